@@ -1,0 +1,527 @@
+// tcgen05 / TMEM / TMA GEMM for sm_100a with the LM step's fused epilogues.
+//
+// C[M,N] = sum_k A[m,k] * B[n,k], bf16 operands, fp32 accumulation in TMEM.
+// Either operand may be K-major ([rows][K]) or MN-major ([K][rows]); the
+// major-ness is a bit of the tcgen05 instruction descriptor plus a different
+// shared-memory descriptor, so the weights are kept once, in the reference's
+// [D_in, D_out] layout (crates/engine/src/layer.rs:16-26), and used as
+//   forward      y  = x  * W    : B MN-major
+//   backward     dx = dy * W^T  : B K-major
+//   weight grad  dW = x^T * dy  : A and B MN-major (contract over tokens)
+// without any transposed copy.
+//
+// Kernel organisation (one CTA per SM, persistent over output tiles):
+//   warp 0      : TMA producer (one lane) -> STAGES-deep smem ring
+//   warp 1      : MMA issuer  (one lane)  -> tcgen05.mma, 128 x BN x 16 per instruction
+//   warp 2      : TMEM allocator (2 x BN fp32 columns: double-buffered accumulator)
+//   warps 4..7  : epilogue, thread t owns accumulator row t (TMEM lane t)
+// The epilogue of tile i overlaps the MMAs of tile i+1.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rt {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 B = one swizzle row
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+struct KParams {
+  int M, N, num_kb;
+  int num_m, num_n, num_tiles;
+  int n_half;
+  int beta;
+  float alpha;
+  int seq, rope_cols;
+  void* out;
+  int64_t ldo;
+  void* out2;
+  int64_t ldo2;
+  const void* aux;
+  int64_t ld_aux;
+  const float* rope_cos;
+  const float* rope_sin;
+  int* err;
+};
+
+__device__ __forceinline__ float silu_sigmoid(float x, float& sig) {
+  sig = 1.f / (1.f + __expf(-x));
+  return x * sig;
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    d[q] = make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                      pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+  }
+}
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u = s[q];
+    v[8 * q + 0] = bf16lo(u.x);
+    v[8 * q + 1] = bf16hi(u.x);
+    v[8 * q + 2] = bf16lo(u.y);
+    v[8 * q + 3] = bf16hi(u.y);
+    v[8 * q + 4] = bf16lo(u.z);
+    v[8 * q + 5] = bf16hi(u.z);
+    v[8 * q + 6] = bf16lo(u.w);
+    v[8 * q + 7] = bf16hi(u.w);
+  }
+}
+
+// Epilogue of one 128 x BN accumulator tile for accumulator row m.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, int m, int tn) {
+  const bool row_ok = m < p.M;
+  if constexpr (EPI == kEpiSwiglu) {
+    // Columns [0, BN/2) hold h1 = x W1, [BN/2, BN) hold h3 = x W3 for the
+    // same BN/2 hidden units (layer.rs / ffn_fused.rs:46-63 semantics).
+    constexpr int HALF = BN / 2;
+#pragma unroll 1
+    for (int c = 0; c < HALF / 32; ++c) {
+      uint32_t g[32], u[32];
+      tmem_ld32(tbase + c * 32, g);
+      tmem_ld32(tbase + HALF + c * 32, u);
+      tmem_ld_wait();
+      const int j = tn * HALF + c * 32;
+      if (row_ok && j < p.N) {
+        float h1[32], h3[32], gate[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          h1[i] = __uint_as_float(g[i]);
+          h3[i] = __uint_as_float(u[i]);
+          float sig;
+          gate[i] = silu_sigmoid(h1[i], sig) * h3[i];
+        }
+        __nv_bfloat16* h13 = static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(m) * p.ldo;
+        store_bf16x32(h13 + j, h1);
+        store_bf16x32(h13 + p.n_half + j, h3);
+        store_bf16x32(static_cast<__nv_bfloat16*>(p.out2) + static_cast<int64_t>(m) * p.ldo2 + j, gate);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tbase + c * 32, r);
+      tmem_ld_wait();
+      const int n = tn * BN + c * 32;
+      if (!row_ok || n >= p.N) continue;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      const int64_t mrow = static_cast<int64_t>(m);
+      if constexpr (EPI == kEpiBf16) {
+        store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
+      } else if constexpr (EPI == kEpiF32 || EPI == kEpiF32Acc || EPI == kEpiResidual) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + mrow * p.ldo + n);
+        if constexpr (EPI == kEpiF32Acc) {
+          if (p.beta) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 o = dst[q];
+              v[4 * q + 0] += o.x;
+              v[4 * q + 1] += o.y;
+              v[4 * q + 2] += o.z;
+              v[4 * q + 3] += o.w;
+            }
+          }
+        }
+        if constexpr (EPI == kEpiResidual) {
+          const float4* res =
+              reinterpret_cast<const float4*>(static_cast<const float*>(p.aux) + mrow * p.ld_aux + n);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 o = res[q];
+            v[4 * q + 0] = o.x + p.alpha * v[4 * q + 0];
+            v[4 * q + 1] = o.y + p.alpha * v[4 * q + 1];
+            v[4 * q + 2] = o.z + p.alpha * v[4 * q + 2];
+            v[4 * q + 3] = o.w + p.alpha * v[4 * q + 3];
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else if constexpr (EPI == kEpiRope) {
+        // Interleaved-pair rotation per head of 128 (kernels/sdpa_fwd.rs:18-33, 100-128):
+        //   y[2i] = x[2i] cos - x[2i+1] sin,  y[2i+1] = x[2i+1] cos + x[2i] sin
+        if (n < p.rope_cols) {
+          const int pos = m % p.seq;
+          const int i0 = (n & 127) >> 1;
+          const float* cs = p.rope_cos + pos * 64 + i0;
+          const float* sn = p.rope_sin + pos * 64 + i0;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const float c = cs[t], s = sn[t];
+            const float x0 = v[2 * t], x1 = v[2 * t + 1];
+            v[2 * t] = x0 * c - x1 * s;
+            v[2 * t + 1] = x1 * c + x0 * s;
+          }
+        }
+        store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
+      } else if constexpr (EPI == kEpiSwigluBwd) {
+        // C = dgate = dffn * W2 (layer.rs:1627-1641); SiLU-gate backward
+        // (layer.rs:1660-1666): dh3 = dg * silu(h1); dh1 = dg * h3 * sig * (1 + h1 (1 - sig)).
+        const __nv_bfloat16* h13 = static_cast<const __nv_bfloat16*>(p.aux) + mrow * p.ld_aux;
+        float h1[32], h3[32];
+        load_bf16x32(h13 + n, h1);
+        load_bf16x32(h13 + p.n_half + n, h3);
+        float dh1[32], dh3[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float sig;
+          const float s = silu_sigmoid(h1[i], sig);
+          const float deriv = sig * (1.f + h1[i] * (1.f - sig));
+          dh3[i] = v[i] * s;
+          dh1[i] = v[i] * h3[i] * deriv;
+        }
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo;
+        store_bf16x32(o + n, dh1);
+        store_bf16x32(o + p.n_half + n, dh3);
+      }
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(256, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const KParams p) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* tfull_bar = empty_bar + C::STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int it = 0;  // stages armed so far
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int tm = tile % p.num_m, tn = tile / p.num_m;
+        const int m0 = tm * BM;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int stage = it % C::STAGES;
+          const uint32_t phase = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
+            set_error(p.err, kDevTimeoutProducer);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          if (*abort_flag) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sA + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          } else {
+            tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              int nphys;
+              if constexpr (EPI == kEpiSwiglu) {
+                constexpr int HALF = BN / 2;
+                nphys = (j < HALF / 64) ? tn * HALF + 64 * j : p.n_half + tn * HALF + 64 * (j - HALF / 64);
+              } else {
+                nphys = tn * BN + 64 * j;
+              }
+              tma_load_2d(sB + j * 8192, &tmB, &full_bar[stage], nphys, k0);
+            }
+          } else {
+            tma_load_2d(sB, &tmB, &full_bar[stage], k0, tn * BN);
+          }
+        }
+      }
+      if (!ok) {
+        // Drain copies that may still be in flight before the CTA exits.
+        for (int i = (it > C::STAGES ? it - C::STAGES : 0); i < it; ++i)
+          mbar_wait(&full_bar[i % C::STAGES], (i / C::STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_par = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_par ^ 1) || *abort_flag) {
+          set_error(p.err, kDevTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int stage = it % C::STAGES;
+          const uint32_t phase = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full_bar[stage], phase) || *abort_flag) {
+            set_error(p.err, kDevTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);  // frees the smem slot once these MMAs finish
+        }
+        if (ok) umma_commit(&tfull_bar[acc]);
+      }
+      // All MMAs issued by this thread must finish before TMEM is released.
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_par = (local >> 1) & 1;
+      bool ok = mbar_wait(&tfull_bar[acc], acc_par);
+      ok = __all_sync(0xffffffffu, ok);
+      const int aborted = __shfl_sync(0xffffffffu, *abort_flag, 0);
+      if (!ok || aborted) {
+        if (!ok && lane == 0) {
+          set_error(p.err, kDevTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      const int tm = tile % p.num_m, tn = tile / p.num_m;
+      const int m = tm * BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue_tile<BN, EPI>(p, tbase, m, tn);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool encoder_ready() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+// 2-D bf16 tensor [outer][inner] with row stride `ld` elements, 128-B swizzled boxes.
+bool make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+               uint32_t box_outer) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+int launch_inst(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid, cudaStream_t s) {
+  using C = GemmCfg<BN>;
+  static const cudaError_t attr = cudaFuncSetAttribute(gemm_tc_kernel<BN, A_MN, B_MN, EPI>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (attr != cudaSuccess) return attr;
+  gemm_tc_kernel<BN, A_MN, B_MN, EPI><<<grid, 256, C::SMEM_BYTES, s>>>(ta, tb, kp);
+  return cudaGetLastError();
+}
+
+template <int BN>
+int dispatch(const GemmArgs& g, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+             cudaStream_t s) {
+#define RT_GEMM_CASE(AMN, BMN, EPI) \
+  if (g.a_mn == AMN && g.b_mn == BMN && g.epi == EPI) return launch_inst<BN, AMN, BMN, EPI>(ta, tb, kp, grid, s);
+  // forward projections (B = weight, MN-major)
+  RT_GEMM_CASE(false, true, kEpiRope)
+  RT_GEMM_CASE(false, true, kEpiResidual)
+  RT_GEMM_CASE(false, true, kEpiSwiglu)
+  RT_GEMM_CASE(false, true, kEpiSwigluBwd)
+  RT_GEMM_CASE(false, true, kEpiF32)
+  RT_GEMM_CASE(false, true, kEpiBf16)
+  RT_GEMM_CASE(false, true, kEpiF32Acc)
+  // K-major weights (W2 forward, logits, data gradients)
+  RT_GEMM_CASE(false, false, kEpiBf16)
+  RT_GEMM_CASE(false, false, kEpiF32)
+  RT_GEMM_CASE(false, false, kEpiF32Acc)
+  RT_GEMM_CASE(false, false, kEpiResidual)
+  RT_GEMM_CASE(false, false, kEpiRope)
+  RT_GEMM_CASE(false, false, kEpiSwigluBwd)
+  // weight gradients: both operands contract over tokens
+  RT_GEMM_CASE(true, true, kEpiF32Acc)
+  RT_GEMM_CASE(true, true, kEpiF32)
+  RT_GEMM_CASE(true, true, kEpiBf16)
+  RT_GEMM_CASE(true, false, kEpiF32)
+  RT_GEMM_CASE(true, false, kEpiF32Acc)
+#undef RT_GEMM_CASE
+  return -1;
+}
+
+int g_num_sms = 0;
+
+}  // namespace
+
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
+  if (!encoder_ready()) return -2;
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.K % BK != 0 || g.N % 32 != 0) return -1;
+  if (g.lda % 8 != 0 || g.ldb % 8 != 0) return -1;
+  if ((reinterpret_cast<uintptr_t>(g.a) | reinterpret_cast<uintptr_t>(g.b) | reinterpret_cast<uintptr_t>(g.out)) & 15)
+    return -1;
+  if (g.a_mn && g.M % 64 != 0) return -1;
+  const bool swiglu = g.epi == kEpiSwiglu;
+  if (swiglu && (!g.b_mn || g.n_half % 64 != 0 || g.N % 64 != 0)) return -1;
+  if (g.epi == kEpiRope && (g.seq <= 0 || g.rope_cols % 128 != 0)) return -1;
+
+  const int sms = num_sms();
+  auto tiles_for = [&](int bn) {
+    const int per_tile_n = swiglu ? bn / 2 : bn;
+    return ((g.M + BM - 1) / BM) * ((g.N + per_tile_n - 1) / per_tile_n);
+  };
+  int bn = g.force_bn;
+  if (bn != 128 && bn != 256) {
+    // Prefer the wide tile unless it leaves noticeably more of the last wave idle.
+    const int t256 = tiles_for(256), t128 = tiles_for(128);
+    const double e256 = double(t256) / (double((t256 + sms - 1) / sms) * sms);
+    const double e128 = double(t128) / (double((t128 + sms - 1) / sms) * sms);
+    bn = (e256 >= 0.85 * e128) ? 256 : 128;
+  }
+  if (swiglu && (g.N % (bn / 2) != 0)) bn = 128;
+
+  KParams kp{};
+  kp.M = g.M;
+  kp.N = g.N;
+  kp.num_kb = g.K / BK;
+  kp.num_m = (g.M + BM - 1) / BM;
+  kp.num_n = swiglu ? (g.N + bn / 2 - 1) / (bn / 2) : (g.N + bn - 1) / bn;
+  kp.num_tiles = kp.num_m * kp.num_n;
+  kp.n_half = g.n_half;
+  kp.beta = g.beta;
+  kp.alpha = g.alpha;
+  kp.seq = g.seq;
+  kp.rope_cols = g.rope_cols;
+  kp.out = g.out;
+  kp.ldo = g.ldo;
+  kp.out2 = g.out2;
+  kp.ldo2 = g.ldo2;
+  kp.aux = g.aux;
+  kp.ld_aux = g.ld_aux;
+  kp.rope_cos = g.rope_cos;
+  kp.rope_sin = g.rope_sin;
+  kp.err = g.err;
+
+  CUtensorMap ta, tb;
+  bool ok;
+  if (g.a_mn)
+    ok = make_tmap(&ta, g.a, g.M, g.K, g.lda, 64, 64);
+  else
+    ok = make_tmap(&ta, g.a, g.K, g.M, g.lda, 64, BM);
+  if (!ok) return -3;
+  const uint64_t b_inner_mn = swiglu ? uint64_t(g.n_half) + g.N : uint64_t(g.N);
+  if (g.b_mn)
+    ok = make_tmap(&tb, g.b, b_inner_mn, g.K, g.ldb, 64, 64);
+  else
+    ok = make_tmap(&tb, g.b, g.K, g.N, g.ldb, 64, bn);
+  if (!ok) return -3;
+
+  const int grid = kp.num_tiles < sms ? kp.num_tiles : sms;
+  return bn == 256 ? dispatch<256>(g, ta, tb, kp, grid, stream) : dispatch<128>(g, ta, tb, kp, grid, stream);
+}
+
+}  // namespace rt

@@ -1,0 +1,170 @@
+"""tcgen05 GEMM parity on the GPU against a plain torch fp32 matmul.
+
+Covers every operand-major combination (K-major / MN-major for A and B), both
+tile widths, ring wrap-around (K > stages * 64), persistent CTAs with more tiles
+than SMs (TMEM double buffer), ragged M/N edges, and each fused epilogue the LM
+step uses.  Inputs are bf16; the reference multiplies the same bf16 values in
+fp32, so only accumulation order differs (tolerance 1e-4 normwise).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from rustane_b200 import _lib  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-30)).item()
+
+
+def rope_tables(seq, hd=128):
+    # crates/engine/src/kernels/sdpa_fwd.rs:18-33, f32 arithmetic
+    p = np.arange(seq, dtype=np.float32)[:, None]
+    i = np.arange(hd // 2, dtype=np.float32)[None, :]
+    theta = p / np.power(np.float32(10000.0), np.float32(2.0) * i / np.float32(hd))
+    return np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+
+
+def gemm(A, a_mn, B, b_mn, M, N, K, epi, out, out2=None, aux=None, alpha=1.0, beta=0, rope=None, seq=0,
+         rope_cols=0, n_half=0, force_bn=0):
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    cos_p = rope[0].data_ptr() if rope is not None else None
+    sin_p = rope[1].data_ptr() if rope is not None else None
+    rc = _lib.lib().rt_kernel_gemm(
+        A.data_ptr(), A.stride(0), int(a_mn), B.data_ptr(), B.stride(0), int(b_mn), M, N, K, epi,
+        out.data_ptr(), out.stride(0), out2.data_ptr() if out2 is not None else None,
+        out2.stride(0) if out2 is not None else 0, aux.data_ptr() if aux is not None else None,
+        aux.stride(0) if aux is not None else 0, alpha, beta, cos_p, sin_p, seq, rope_cols, n_half, force_bn,
+        err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0, rc
+    assert err.item() == 0, err.item()
+
+
+def operands(M, N, K, a_mn, b_mn, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    A = torch.randn((K, M) if a_mn else (M, K), generator=g, device="cuda").bfloat16()
+    B = torch.randn((K, N) if b_mn else (N, K), generator=g, device="cuda").bfloat16()
+    A_log = A.t() if a_mn else A
+    B_log = B.t() if b_mn else B
+    ref = A_log.float() @ B_log.float().t()
+    return A, B, ref
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_majors_f32(a_mn, b_mn, bn):
+    M, N, K = 256, 512, 448
+    A, B, ref = operands(M, N, K, a_mn, b_mn)
+    out = torch.empty(M, N, device="cuda")
+    gemm(A, a_mn, B, b_mn, M, N, K, _lib.EPI_F32, out, force_bn=bn)
+    assert _rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_persistent_many_tiles(bn):
+    # more tiles than SMs: every CTA cycles both TMEM accumulators several times
+    M, N, K = 2048, 4096, 256
+    A, B, ref = operands(M, N, K, False, True, seed=1)
+    out = torch.empty(M, N, device="cuda")
+    gemm(A, False, B, True, M, N, K, _lib.EPI_F32, out, force_bn=bn)
+    assert _rel(out, ref) < TOL
+
+
+def test_gemm_ragged_edges():
+    # M not a multiple of 128 and N not a multiple of the tile width
+    M, N, K = 200, 352, 192
+    A, B, ref = operands(M, N, K, False, False, seed=2)
+    out = torch.full((M, N), 7.0, device="cuda")
+    gemm(A, False, B, False, M, N, K, _lib.EPI_F32, out)
+    assert _rel(out, ref) < TOL
+
+
+def test_gemm_bf16_out():
+    M, N, K = 384, 768, 512
+    A, B, ref = operands(M, N, K, False, True, seed=3)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    gemm(A, False, B, True, M, N, K, _lib.EPI_BF16, out)
+    assert _rel(out, ref) < 8e-3
+
+
+@pytest.mark.parametrize("beta", [0, 1])
+def test_gemm_f32_accumulate(beta):
+    M, N, K = 256, 384, 1024
+    A, B, ref = operands(M, N, K, True, True, seed=4)
+    out = torch.randn(M, N, device="cuda")
+    base = out.clone()
+    gemm(A, True, B, True, M, N, K, _lib.EPI_F32_ACC, out, beta=beta)
+    expect = ref + base if beta else ref
+    assert _rel(out, expect) < TOL
+
+
+def test_gemm_residual():
+    M, N, K = 512, 768, 768
+    A, B, ref = operands(M, N, K, False, True, seed=5)
+    resid = torch.randn(M, N, device="cuda")
+    out = torch.empty(M, N, device="cuda")
+    alpha = 0.1581
+    gemm(A, False, B, True, M, N, K, _lib.EPI_RESIDUAL, out, aux=resid, alpha=alpha)
+    assert _rel(out, resid + alpha * ref) < TOL
+
+
+def test_gemm_rope_qkv():
+    seq, D, B = 256, 256, 2
+    M, N, K = B * seq, 3 * D, 256
+    A, Bw, ref = operands(M, N, K, False, True, seed=6)
+    cos, sin = rope_tables(seq)
+    rope = (torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda())
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    gemm(A, False, Bw, True, M, N, K, _lib.EPI_ROPE, out, rope=rope, seq=seq, rope_cols=2 * D)
+    exp = ref.clone()
+    pos = torch.arange(M, device="cuda") % seq
+    c = rope[0][pos].repeat(1, 2 * D // 128)  # [M, D] pairs
+    s = rope[1][pos].repeat(1, 2 * D // 128)
+    x0 = ref[:, 0:2 * D:2]
+    x1 = ref[:, 1:2 * D:2]
+    exp[:, 0:2 * D:2] = x0 * c - x1 * s
+    exp[:, 1:2 * D:2] = x1 * c + x0 * s
+    assert _rel(out, exp) < 8e-3
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_swiglu(bn):
+    M, D, H = 512, 256, 640
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(M, D, generator=g, device="cuda").bfloat16()
+    w13 = (0.1 * torch.randn(D, 2 * H, generator=g, device="cuda")).bfloat16()  # [D, w1 | w3]
+    h13 = torch.empty(M, 2 * H, device="cuda", dtype=torch.bfloat16)
+    gate = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    gemm(x, False, w13, True, M, H, D, _lib.EPI_SWIGLU, h13, out2=gate, n_half=H, force_bn=bn)
+    h = x.float() @ w13.float()
+    h1, h3 = h[:, :H], h[:, H:]
+    assert _rel(h13[:, :H], h1) < 8e-3
+    assert _rel(h13[:, H:], h3) < 8e-3
+    assert _rel(gate, torch.nn.functional.silu(h1) * h3) < 8e-3
+
+
+def test_gemm_swiglu_bwd():
+    M, D, H = 256, 256, 384
+    g = torch.Generator(device="cuda").manual_seed(8)
+    dffn = torch.randn(M, D, generator=g, device="cuda").bfloat16()
+    w2 = (0.1 * torch.randn(D, H, generator=g, device="cuda")).bfloat16()  # reference layout [D, H]
+    h13 = torch.randn(M, 2 * H, generator=g, device="cuda").bfloat16()
+    dh13 = torch.empty(M, 2 * H, device="cuda", dtype=torch.bfloat16)
+    gemm(dffn, False, w2, True, M, H, D, _lib.EPI_SWIGLU_BWD, dh13, aux=h13, n_half=H)
+    dg = dffn.float() @ w2.float()
+    h1, h3 = h13[:, :H].float(), h13[:, H:].float()
+    sig = torch.sigmoid(h1)
+    dh3 = dg * h1 * sig
+    dh1 = dg * h3 * sig * (1 + h1 * (1 - sig))
+    assert _rel(dh13[:, :H], dh1) < 8e-3
+    assert _rel(dh13[:, H:], dh3) < 8e-3
