@@ -16,8 +16,15 @@
  *    non-zero status back to that panic).
  *  - Host pointers are borrowed for the duration of the call only.  Device
  *    memory is owned by the context.  Calls on one context are not thread-safe.
- *  - Host tensors use the reference layouts: row-major fp32, wq/wk/wv/wo
- *    [dim, dim], w1/w3/w2 [dim, hidden], embed [vocab, dim], gammas [dim].
+ *    Model-level calls are synchronous at return.
+ *  - Host tensors use the reference layouts: row-major fp32, wq/wk/wv [dim,
+ *    q_dim|kv_dim], wo [q_dim, dim], w1/w3/w2 [dim, hidden], embed [vocab, dim],
+ *    gammas [dim].  Token ids are uint32 (the reference's u16 data files are
+ *    widened by the caller, crates/engine/src/full_model.rs:683-684).
+ *  - A batch is `batch` sequences of cfg.seq tokens each, processed in one
+ *    pass; gradients are the SUM over sequences, exactly as the reference's
+ *    gradient accumulation over `accum_steps` microbatches
+ *    (full_model.rs:680-694), and the returned loss is the MEAN over sequences.
  *  - rt_kernel_* entry points take DEVICE pointers and a cudaStream_t (as
  *    void*); they launch one kernel asynchronously and exist for kernel-level
  *    parity checks.
@@ -49,7 +56,141 @@ extern "C" {
 #define RT_ERR_STATE (-8)      /* call order (e.g. backward before forward)   */
 #define RT_ERR_NONFINITE (-9)  /* loss or gradient norm is NaN / Inf          */
 
-/* GEMM epilogue selector for rt_kernel_gemm (see the kernel sources). */
+/* rt_ctx_create flags */
+#define RT_CTX_TRAIN 0        /* fp32 master weights, grads, Adam moments, cached activations */
+#define RT_CTX_FORWARD_ONLY 1 /* bf16 weights only, activations reused layer to layer        */
+
+/* rt_dist_init modes */
+#define RT_DIST_DATA_PARALLEL 0   /* gradients all-reduced (sum) before grad-norm / AdamW */
+#define RT_DIST_TENSOR_PARALLEL 1 /* forward-only: heads / hidden sharded, all-reduce after Wo and W2 */
+
+/* ----------------------------------------------------------------- types */
+
+/* crates/engine/src/model.rs:5-17 (ModelConfig). */
+typedef struct rt_model_config {
+  int32_t dim, hidden, heads, kv_heads, hd, seq, nlayers, vocab, q_dim, kv_dim, gqa_ratio;
+} rt_model_config;
+
+/* crates/engine/src/full_model.rs:34-70 (TrainConfig). */
+typedef struct rt_train_config {
+  float max_lr, min_lr_frac;
+  uint32_t warmup_steps, total_steps;
+  float beta1, beta2, eps, weight_decay, matrix_lr_scale, embed_lr_scale, loss_scale;
+  uint32_t accum_steps;
+  float grad_clip, softcap;
+} rt_train_config;
+
+/* Per-layer host tensors (crates/engine/src/layer.rs:16-39 LayerWeights /
+ * LayerGrads; training.rs:11-21 LayerOptState uses the same shapes). */
+typedef struct rt_layer_ptrs {
+  float *wq, *wk, *wv, *wo, *w1, *w3, *w2, *gamma1, *gamma2;
+} rt_layer_ptrs;
+
+/* Whole-model host tensors (full_model.rs:13-31 ModelWeights / ModelGrads /
+ * ModelOptState); `layers` points to cfg.nlayers entries. */
+typedef struct rt_model_ptrs {
+  float* embed;
+  float* gamma_final;
+  rt_layer_ptrs* layers;
+} rt_model_ptrs;
+
+/* Device-side phase and kernel timings (CUDA events on the context stream). */
+typedef struct rt_timings {
+  double fwd_ms, bwd_ms, comm_ms, opt_ms; /* last forward / backward / all-reduce / norm+AdamW */
+  double gemm_ms, gemm_flops;             /* accumulated over GEMM launches while profiling   */
+  double attn_ms, attn_flops;             /* accumulated over attention launches              */
+  double other_ms;                        /* accumulated over all other kernels               */
+  int64_t gemm_launches, attn_launches, other_launches;
+  int64_t kernel_launches; /* every kernel this context launched since creation */
+} rt_timings;
+
+typedef struct rt_ctx rt_ctx;
+
+/* --------------------------------------------------------- context / data */
+
+/* Allocate a context on `device` for batches of up to `max_batch` sequences.
+ * Replaces CompiledKernels::compile (crates/engine/src/layer.rs:237-275) plus
+ * the workspaces ModelForwardWorkspace / ModelBackwardWorkspace
+ * (full_model.rs:123-185). */
+RT_API int rt_ctx_create(const rt_model_config* cfg, int device, int max_batch, int flags, rt_ctx** out);
+RT_API int rt_ctx_destroy(rt_ctx* ctx);
+RT_API const char* rt_last_error(const rt_ctx* ctx);
+/* Bytes of device memory the context holds. */
+RT_API int rt_ctx_device_bytes(const rt_ctx* ctx, int64_t* out);
+
+/* Copy weights host -> device (fp32 master + bf16 compute copy). */
+RT_API int rt_weights_upload(rt_ctx* ctx, const rt_model_ptrs* w);
+/* Copy weights device -> host (fp32 master; training contexts only). */
+RT_API int rt_weights_download(rt_ctx* ctx, const rt_model_ptrs* w);
+/* Gradients device <-> host (reference layout, ModelGrads). */
+RT_API int rt_grads_download(rt_ctx* ctx, const rt_model_ptrs* g);
+RT_API int rt_grads_upload(rt_ctx* ctx, const rt_model_ptrs* g);
+/* Adam moments device <-> host (ModelOptState). */
+RT_API int rt_opt_download(rt_ctx* ctx, const rt_model_ptrs* m, const rt_model_ptrs* v);
+RT_API int rt_opt_upload(rt_ctx* ctx, const rt_model_ptrs* m, const rt_model_ptrs* v);
+/* Device-side init: every matrix and the embedding N(0, std) from a counter-based
+ * stream keyed by `seed`, gammas = 1, moments and gradients 0.  Used for the
+ * configurations whose fp32 weights do not fit comfortably in host memory. */
+RT_API int rt_weights_init_normal(rt_ctx* ctx, uint64_t seed, float std);
+
+/* Host-side helper: the reference's LCG init stream (random_vec,
+ * crates/engine/src/layer.rs:404-413): seed = 42 + n. */
+RT_API int rt_lcg_fill(float* out, int64_t n, float scale);
+
+/* ---------------------------------------------------------- model step */
+
+/* Forward of `batch` sequences + cross-entropy (full_model::forward_ws,
+ * full_model.rs:187-247; per_token_loss = forward_losses, :717-767).
+ * tokens / targets: batch * seq uint32 ids.  loss_out: mean loss.
+ * per_token_loss (nullable): batch * seq CE values.  Keeps the activations
+ * for rt_backward (training contexts). */
+RT_API int rt_forward(rt_ctx* ctx, const uint32_t* tokens, const uint32_t* targets, int batch, float softcap,
+                      float* loss_out, float* per_token_loss);
+/* Copy the last forward's logits (after softcap) to host, [batch*seq, vocab] fp32. */
+RT_API int rt_logits_download(rt_ctx* ctx, float* logits);
+/* Backward of the last forward (full_model::backward_ws, full_model.rs:250-331):
+ * dlogits * loss_scale, gradients accumulate into the device grads. */
+RT_API int rt_backward(rt_ctx* ctx, float softcap, float loss_scale);
+/* ModelGrads::zero_out (full_model.rs:100-107). */
+RT_API int rt_grads_zero(rt_ctx* ctx);
+/* Global L2 norm of all gradients (grad_norm, full_model.rs:598-624). */
+RT_API int rt_grad_norm(rt_ctx* ctx, float* norm_out);
+/* clip_grads (full_model.rs:627-645). */
+RT_API int rt_clip_grads(rt_ctx* ctx, float max_norm);
+/* AdamW with the reference's learning-rate groups (update_weights,
+ * full_model.rs:490-593): embed lr*embed_lr_scale wd 0, gamma_final lr wd 0,
+ * matrices lr*matrix_lr_scale wd weight_decay, gamma1/2 lr wd 0; t is 1-based. */
+RT_API int rt_update_weights(rt_ctx* ctx, uint32_t t, float lr, const rt_train_config* tc, float grad_scale);
+/* learning_rate (full_model.rs:334-342). */
+RT_API float rt_learning_rate(uint32_t step, const rt_train_config* tc);
+/* One optimizer step over `batch` sequences (train_step, full_model.rs:661-714,
+ * with accum_steps = batch * world): zero grads, forward, backward with
+ * tc->loss_scale, [data-parallel all-reduce], grad norm, clip rule, lr(step),
+ * AdamW(t = step + 1).  The clip decision runs on the device (no host sync
+ * inside the step).  loss_out: mean loss of this rank's sequences. */
+RT_API int rt_train_step(rt_ctx* ctx, const uint32_t* tokens, const uint32_t* targets, int batch, uint32_t step,
+                         const rt_train_config* tc, float* loss_out);
+
+/* ------------------------------------------------------- multi-GPU */
+
+/* NCCL unique id (128 bytes) for rank 0 to broadcast to the other ranks. */
+RT_API int rt_nccl_unique_id(uint8_t* out128);
+/* Join a communicator of `world` ranks (one process per GPU).  mode:
+ * RT_DIST_DATA_PARALLEL or RT_DIST_TENSOR_PARALLEL.  Collectives that do not
+ * finish within timeout_ms abort the communicator and return RT_ERR_NCCL. */
+RT_API int rt_dist_init(rt_ctx* ctx, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms);
+/* Sum the gradients over the data-parallel ranks (one in-place all-reduce). */
+RT_API int rt_grad_allreduce(rt_ctx* ctx);
+
+/* ------------------------------------------------------- diagnostics */
+
+/* Enable (1) / disable (0) per-kernel CUDA-event timing; resets the accumulators. */
+RT_API int rt_profile(rt_ctx* ctx, int enable);
+RT_API int rt_get_timings(rt_ctx* ctx, rt_timings* out);
+
+/* -------------------------------------------------- kernel-level entries */
+
+/* GEMM epilogue selector for rt_kernel_gemm. */
 #define RT_EPI_BF16 0
 #define RT_EPI_F32 1
 #define RT_EPI_F32_ACC 2
@@ -57,8 +198,6 @@ extern "C" {
 #define RT_EPI_ROPE 4
 #define RT_EPI_SWIGLU 5
 #define RT_EPI_SWIGLU_BWD 6
-
-/* -------------------------------------------------- kernel-level entries */
 
 /* tcgen05 GEMM C[M,N] = sum_k A[m,k] B[n,k] (bf16 in, fp32 accumulate) with a
  * fused epilogue.  a_mn/b_mn select MN-major storage ([K][M] / [K][N]).
@@ -70,6 +209,51 @@ RT_API int rt_kernel_gemm(const void* a, int64_t lda, int a_mn, const void* b, i
                           int K, int epi, void* out, int64_t ldo, void* out2, int64_t ldo2, const void* aux,
                           int64_t ld_aux, float alpha, int beta, const float* rope_cos, const float* rope_sin,
                           int seq, int rope_cols, int n_half, int force_bn, int* dev_err, void* stream);
+
+/* Causal attention forward over qkv [batch*seq, 3*dim] bf16 (roped Q, K; V):
+ * out [batch*seq, dim] bf16, lse2 [batch, heads, seq] fp32 (log2 domain).
+ * Replaces the attention half of sdpaFwd (kernels/sdpa_fwd.rs:130-150). */
+RT_API int rt_kernel_attention_fwd(const void* qkv, void* out, float* lse2, int batch, int seq, int heads,
+                                   void* stream);
+/* Causal attention backward: dqkv [batch*seq, 3*dim] bf16 with the RoPE backward
+ * rotation applied to dQ and dK (rope tables [hd/2][seq], layer.rs:197-217).
+ * dvec: scratch [batch, heads, seq] fp32.  Replaces sdpaBwd1 + sdpaBwd2
+ * (kernels/sdpa_bwd.rs:44-162) and rope_backward_inplace (layer.rs:1880-1897). */
+RT_API int rt_kernel_attention_bwd(const void* qkv, const void* out, const float* lse2, const void* dout,
+                                   float* dvec, void* dqkv, const float* rope_cos_b, const float* rope_sin_b,
+                                   int batch, int seq, int heads, void* stream);
+
+/* Row RMSNorm over x [M, D] fp32 -> out bf16, rms_inv [M]
+ * (cpu/rmsnorm.rs:149-183, token-major). */
+RT_API int rt_kernel_rmsnorm_fwd(const float* x, const float* gamma, void* out_bf16, float* rms_inv, int M, int D,
+                                 void* stream);
+/* RMSNorm backward (cpu/rmsnorm.rs:190-238, token-major): dx = ... + resid,
+ * optional dx_bf16 = bf16(scale * dx); dgamma (accumulate ? += : =).
+ * partials: scratch of rt_kernel_rmsnorm_bwd_partials(M) * D floats. */
+RT_API int rt_kernel_rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float* rms_inv,
+                                 const float* resid, float* dx, void* dx_bf16, float bf16_scale, float* dgamma,
+                                 int accumulate, float* partials, int M, int D, void* stream);
+RT_API int rt_kernel_rmsnorm_bwd_partials(int M);
+/* Embedding gather (cpu/embedding.rs:8-16): x[m,:] = E[tok[m],:] exactly. */
+RT_API int rt_kernel_embed_gather(const float* E, const uint32_t* tok, float* x, int M, int D, int V, int* dev_err,
+                                  void* stream);
+/* Embedding scatter-add (cpu/embedding.rs:34-44), deterministic: segments of
+ * positions grouped by token (perm, seg_start[nseg+1], seg_tok[nseg]). */
+RT_API int rt_kernel_embed_scatter(const float* dx, const int32_t* perm, const int32_t* seg_start,
+                                   const uint32_t* seg_tok, int nseg, float* dE, int D, void* stream);
+/* Cross-entropy forward / backward over fp32 logits rows (cpu/cross_entropy.rs:58-96,
+ * softcap full_model.rs:232-239, 265-276). */
+RT_API int rt_kernel_ce_fwd(const float* logits, const uint32_t* tgt, float* row_loss, float* row_lse, int M, int V,
+                            float softcap, void* stream);
+RT_API int rt_kernel_ce_bwd(const float* logits, const float* row_lse, const uint32_t* tgt, void* dl_bf16, int M,
+                            int V, float softcap, float scale, void* stream);
+/* Multi-tensor AdamW over one contiguous fp32 range (cpu/adam.rs:95-132),
+ * optional bf16 copy of the updated parameters. */
+RT_API int rt_kernel_adam(float* param, const float* grad, float* m, float* v, void* param_bf16, int64_t n,
+                          uint32_t t, float lr, float beta1, float beta2, float eps, float weight_decay,
+                          float grad_scale, void* stream);
+/* Deterministic global L2 norm; partials: scratch of 1024 floats. */
+RT_API int rt_kernel_l2norm(const float* x, int64_t n, float* partials, float* out_norm, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,30 @@
+// Launch interface of the causal attention kernels (internal).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rt {
+
+struct AttnArgs {
+  int batch = 0, S = 0, heads = 0, hd = 128, D = 0;
+  const __nv_bfloat16* qkv = nullptr;  // [M, ldq]: Q | K | V, roped Q and K
+  int64_t ldq = 0;
+  __nv_bfloat16* out = nullptr;  // forward: O [M, ldo]; backward: O (input)
+  int64_t ldo = 0;
+  float* lse2 = nullptr;  // [batch, heads, S] log2-domain softmax statistic
+  // backward only
+  const __nv_bfloat16* dout = nullptr;  // dO [M, lddo]
+  int64_t lddo = 0;
+  float* dvec = nullptr;  // [batch, heads, S] scratch: rowsum(dO * O)
+  __nv_bfloat16* dqkv = nullptr;  // [M, lddq]: dQ | dK | dV (RoPE backward applied)
+  int64_t lddq = 0;
+  const float* rope_cos_b = nullptr;  // [hd/2][S]
+  const float* rope_sin_b = nullptr;
+};
+
+int attn_forward(const AttnArgs& a, cudaStream_t s);
+int attn_backward(const AttnArgs& a, cudaStream_t s);
+
+}  // namespace rt

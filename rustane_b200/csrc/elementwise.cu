@@ -1,0 +1,528 @@
+// Memory-bound kernels of the LM step: 128-bit vector loads/stores, warp-shuffle
+// reductions, fixed-order (deterministic) cross-block reductions.
+#include "common.cuh"
+#include "elementwise.h"
+
+namespace rt {
+namespace {
+
+constexpr float kRmsEps = 1e-5f;  // crates/engine/src/cpu/rmsnorm.rs:10
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// Block-wide sum in fixed order; result broadcast to all threads. `red` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = lane < nw ? red[lane] : 0.f;
+  r = warp_sum(r);
+  return r;
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = lane < nw ? red[lane] : -INFINITY;
+  return warp_max(r);
+}
+
+// ------------------------------------------------------------- embedding
+__global__ void embed_gather_kernel(const float* __restrict__ E, const uint32_t* __restrict__ tok,
+                                    float* __restrict__ x, int M, int D, int V, int* err) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const uint32_t t = tok[row];
+  float4* dst = reinterpret_cast<float4*>(x + static_cast<int64_t>(row) * D);
+  const int D4 = D >> 2;
+  if (t >= static_cast<uint32_t>(V)) {
+    if (lane == 0) set_error(err, kDevBadToken);
+    for (int c = lane; c < D4; c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(E + static_cast<int64_t>(t) * D);
+  for (int c = lane; c < D4; c += 32) dst[c] = src[c];
+}
+
+__global__ void embed_scatter_kernel(const float* __restrict__ dx, const int32_t* __restrict__ perm,
+                                     const int32_t* __restrict__ seg_start, const uint32_t* __restrict__ seg_tok,
+                                     float* __restrict__ dE, int D) {
+  const int j = blockIdx.x;
+  const int b = seg_start[j], e = seg_start[j + 1];
+  float4* row = reinterpret_cast<float4*>(dE + static_cast<int64_t>(seg_tok[j]) * D);
+  const int D4 = D >> 2;
+  for (int c = threadIdx.x; c < D4; c += blockDim.x) {
+    float4 acc = row[c];
+    for (int i = b; i < e; ++i) {  // positions in ascending order (embedding.rs:34-44)
+      const float4 v = reinterpret_cast<const float4*>(dx + static_cast<int64_t>(perm[i]) * D)[c];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    row[c] = acc;
+  }
+}
+
+// --------------------------------------------------------------- RMSNorm
+__global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                   __nv_bfloat16* __restrict__ out, float* __restrict__ rms_inv, int M, int D) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(row) * D);
+  const int D4 = D >> 2;
+  float ss = 0.f;
+  for (int c = lane; c < D4; c += 32) {
+    const float4 v = xr[c];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(D)) + kRmsEps);
+  if (lane == 0) rms_inv[row] = r;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * D);
+  for (int c = lane; c < D4; c += 32) {
+    const float4 v = xr[c], g = g4[c];
+    o[c] = make_uint2(pack_bf16x2(v.x * r * g.x, v.y * r * g.y), pack_bf16x2(v.z * r * g.z, v.w * r * g.w));
+  }
+}
+
+constexpr int kBwdRows = 16;   // rows per block (dgamma partial granularity)
+constexpr int kBwdThreads = 256;
+constexpr int kBwdVec = 8;     // float4 per thread -> D <= 8192
+
+__global__ void __launch_bounds__(kBwdThreads)
+    rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
+                       const float* __restrict__ rms_inv, const float* __restrict__ resid, float* __restrict__ dx,
+                       __nv_bfloat16* __restrict__ dx_bf16, float bf16_scale, float* __restrict__ dgamma_part, int M,
+                       int D) {
+  __shared__ float red[32];
+  const int D4 = D >> 2;
+  const int tid = threadIdx.x;
+  float4 g[kBwdVec], dga[kBwdVec];
+#pragma unroll
+  for (int j = 0; j < kBwdVec; ++j) {
+    const int c = tid + j * kBwdThreads;
+    g[j] = c < D4 ? reinterpret_cast<const float4*>(gamma)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    dga[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float inv_dim = 1.0f / static_cast<float>(D);
+  const int m0 = blockIdx.x * kBwdRows;
+  for (int m = m0; m < m0 + kBwdRows && m < M; ++m) {
+    const float r = rms_inv[m];
+    const float4* dyr = reinterpret_cast<const float4*>(dy + static_cast<int64_t>(m) * D);
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(m) * D);
+    float4 dyv[kBwdVec], xh[kBwdVec];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < kBwdVec; ++j) {
+      const int c = tid + j * kBwdThreads;
+      if (c < D4) {
+        dyv[j] = dyr[c];
+        const float4 xv = xr[c];
+        xh[j] = make_float4(xv.x * r, xv.y * r, xv.z * r, xv.w * r);
+        dot += dyv[j].x * g[j].x * xh[j].x + dyv[j].y * g[j].y * xh[j].y + dyv[j].z * g[j].z * xh[j].z +
+               dyv[j].w * g[j].w * xh[j].w;
+      }
+    }
+    dot = block_sum(dot, red) * inv_dim;
+    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<int64_t>(m) * D);
+    const float4* rr = resid ? reinterpret_cast<const float4*>(resid + static_cast<int64_t>(m) * D) : nullptr;
+    uint2* ob = dx_bf16 ? reinterpret_cast<uint2*>(dx_bf16 + static_cast<int64_t>(m) * D) : nullptr;
+#pragma unroll
+    for (int j = 0; j < kBwdVec; ++j) {
+      const int c = tid + j * kBwdThreads;
+      if (c < D4) {
+        float4 o;
+        o.x = r * (dyv[j].x * g[j].x - xh[j].x * dot);
+        o.y = r * (dyv[j].y * g[j].y - xh[j].y * dot);
+        o.z = r * (dyv[j].z * g[j].z - xh[j].z * dot);
+        o.w = r * (dyv[j].w * g[j].w - xh[j].w * dot);
+        if (rr) {
+          const float4 q = rr[c];
+          o.x += q.x;
+          o.y += q.y;
+          o.z += q.z;
+          o.w += q.w;
+        }
+        dxr[c] = o;
+        if (ob)
+          ob[c] = make_uint2(pack_bf16x2(o.x * bf16_scale, o.y * bf16_scale),
+                             pack_bf16x2(o.z * bf16_scale, o.w * bf16_scale));
+        dga[j].x += dyv[j].x * xh[j].x;
+        dga[j].y += dyv[j].y * xh[j].y;
+        dga[j].z += dyv[j].z * xh[j].z;
+        dga[j].w += dyv[j].w * xh[j].w;
+      }
+    }
+  }
+  float4* part = reinterpret_cast<float4*>(dgamma_part + static_cast<int64_t>(blockIdx.x) * D);
+#pragma unroll
+  for (int j = 0; j < kBwdVec; ++j) {
+    const int c = tid + j * kBwdThreads;
+    if (c < D4) part[c] = dga[j];
+  }
+}
+
+__global__ void dgamma_reduce_kernel(const float* __restrict__ part, int nblk, float* __restrict__ dgamma, int D,
+                                     int accumulate) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float s = 0.f;
+  for (int b = 0; b < nblk; ++b) s += part[static_cast<int64_t>(b) * D + d];
+  dgamma[d] = accumulate ? dgamma[d] + s : s;
+}
+
+// --------------------------------------------------------- cross-entropy
+constexpr int kCeThreads = 256;
+constexpr int kCeVec = 8;  // float4 per thread -> V <= 8192
+
+__device__ __forceinline__ float capz(float l, float softcap) {
+  return softcap > 0.f ? softcap * tanhf(l * (1.0f / softcap)) : l;
+}
+
+__global__ void __launch_bounds__(kCeThreads)
+    ce_forward_kernel(const float* __restrict__ logits, const uint32_t* __restrict__ tgt, float* __restrict__ row_loss,
+                      float* __restrict__ row_lse, int V, float softcap) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const float4* lr = reinterpret_cast<const float4*>(logits + static_cast<int64_t>(m) * V);
+  const int V4 = V >> 2;
+  float4 z[kCeVec];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kCeVec; ++j) {
+    const int c = threadIdx.x + j * kCeThreads;
+    if (c < V4) {
+      float4 v = lr[c];
+      v.x = capz(v.x, softcap);
+      v.y = capz(v.y, softcap);
+      v.z = capz(v.z, softcap);
+      v.w = capz(v.w, softcap);
+      z[j] = v;
+      mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+  }
+  mx = block_max(mx, red);
+  float se = 0.f;
+#pragma unroll
+  for (int j = 0; j < kCeVec; ++j) {
+    const int c = threadIdx.x + j * kCeThreads;
+    if (c < V4) se += __expf(z[j].x - mx) + __expf(z[j].y - mx) + __expf(z[j].z - mx) + __expf(z[j].w - mx);
+  }
+  se = block_sum(se, red);
+  if (threadIdx.x == 0) {
+    const float lse = mx + logf(se);
+    const uint32_t t = tgt[m];
+    row_lse[m] = lse;
+    row_loss[m] = lse - capz(logits[static_cast<int64_t>(m) * V + t], softcap);
+  }
+}
+
+__global__ void __launch_bounds__(kCeThreads)
+    ce_backward_kernel(const float* __restrict__ logits, const float* __restrict__ row_lse,
+                       const uint32_t* __restrict__ tgt, __nv_bfloat16* __restrict__ dl, int V, float softcap,
+                       float scale) {
+  const int m = blockIdx.x;
+  const float4* lr = reinterpret_cast<const float4*>(logits + static_cast<int64_t>(m) * V);
+  uint2* o = reinterpret_cast<uint2*>(dl + static_cast<int64_t>(m) * V);
+  const int V4 = V >> 2;
+  const float lse = row_lse[m];
+  const int t = static_cast<int>(tgt[m]);
+  for (int c = threadIdx.x; c < V4; c += kCeThreads) {
+    const float4 v = lr[c];
+    float l[4] = {v.x, v.y, v.z, v.w};
+    float d[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float z = l[e], dz = 1.f;
+      if (softcap > 0.f) {
+        const float th = tanhf(l[e] * (1.0f / softcap));
+        z = softcap * th;
+        dz = 1.f - th * th;  // full_model.rs:267-273
+      }
+      float p = __expf(z - lse);
+      if (4 * c + e == t) p -= 1.f;
+      d[e] = p * scale * dz;
+    }
+    o[c] = make_uint2(pack_bf16x2(d[0], d[1]), pack_bf16x2(d[2], d[3]));
+  }
+}
+
+__global__ void mean_reduce_kernel(const float* __restrict__ x, int n, float* __restrict__ out) {
+  __shared__ double red[32];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    double r = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (lane == 0) out[0] = static_cast<float>(r / n);
+  }
+}
+
+// ---------------------------------------------------------- grad norm
+constexpr int kNormBlocks = 1024;
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) sumsq_partial_kernel(const float* __restrict__ x, int64_t n,
+                                                                      float* __restrict__ partials) {
+  __shared__ double red[32];
+  const int64_t n4 = n >> 2;
+  const int64_t per = (n4 + gridDim.x - 1) / gridDim.x;
+  const int64_t b = per * blockIdx.x, e = min(n4, b + per);
+  float s = 0.f;
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  if (blockIdx.x == gridDim.x - 1)  // tail elements not covered by float4s
+    for (int64_t i = (n4 << 2) + threadIdx.x; i < n; i += blockDim.x) s += x[i] * x[i];
+  double d = s;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = d;
+  __syncthreads();
+  if (warp == 0) {
+    double r = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (lane == 0) partials[blockIdx.x] = static_cast<float>(r);
+  }
+}
+
+__global__ void sumsq_final_kernel(const float* __restrict__ partials, int n, float* __restrict__ out) {
+  __shared__ double red[32];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += partials[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    double r = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (lane == 0) out[0] = static_cast<float>(sqrt(r));
+  }
+}
+
+// ----------------------------------------------------------------- AdamW
+struct AdamKParams {
+  AdamSegment seg[4];
+  int nseg;
+  float beta1, beta2, eps, bc1, bc2, grad_scale, gsc, clip;
+};
+
+__global__ void __launch_bounds__(256) adam_kernel(float* __restrict__ param, const float* __restrict__ grad,
+                                                   float* __restrict__ m, float* __restrict__ v,
+                                                   __nv_bfloat16* __restrict__ pb, const float* __restrict__ norm,
+                                                   const AdamKParams k) {
+  float scale = k.grad_scale;
+  if (norm) {  // full_model.rs:696-704
+    const float raw = *norm;
+    scale = (k.clip > 0.f && raw * k.gsc > k.clip) ? k.clip / raw : k.gsc;
+  }
+  const float omb1 = 1.0f - k.beta1, omb2 = 1.0f - k.beta2;
+  for (int s = 0; s < k.nseg; ++s) {
+    const AdamSegment sg = k.seg[s];
+    const int64_t b4 = sg.begin >> 2, e4 = sg.end >> 2;
+    for (int64_t i = b4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < e4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const float4 g4 = reinterpret_cast<const float4*>(grad)[i];
+      float4 p4 = reinterpret_cast<float4*>(param)[i];
+      float4 m4 = reinterpret_cast<float4*>(m)[i];
+      float4 v4 = reinterpret_cast<float4*>(v)[i];
+      float gg[4] = {g4.x, g4.y, g4.z, g4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w}, mm[4] = {m4.x, m4.y, m4.z, m4.w},
+            vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {  // crates/engine/src/cpu/adam.rs:119-131
+        const float g = gg[e] * scale;
+        const float mi = k.beta1 * mm[e] + omb1 * g;
+        const float vi = k.beta2 * vv[e] + omb2 * g * g;
+        mm[e] = mi;
+        vv[e] = vi;
+        const float mh = mi * k.bc1, vh = vi * k.bc2;
+        const float upd = mh / (sqrtf(vh) + k.eps);
+        pp[e] -= sg.lr * (upd + sg.wd * pp[e]);
+      }
+      reinterpret_cast<float4*>(param)[i] = make_float4(pp[0], pp[1], pp[2], pp[3]);
+      reinterpret_cast<float4*>(m)[i] = make_float4(mm[0], mm[1], mm[2], mm[3]);
+      reinterpret_cast<float4*>(v)[i] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      if (sg.write_bf16)
+        reinterpret_cast<uint2*>(pb)[i] = make_uint2(pack_bf16x2(pp[0], pp[1]), pack_bf16x2(pp[2], pp[3]));
+    }
+  }
+}
+
+// ---------------------------------------------------------------- misc
+__global__ void cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n4) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    reinterpret_cast<uint2*>(dst)[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+__global__ void fill_kernel(float* __restrict__ dst, int64_t n, float value) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = value;
+}
+__global__ void scale_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n, float a) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[i] = a * x[i];
+}
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+// Box-Muller on two 24-bit uniforms per pair of elements.
+__global__ void init_normal_kernel(float* __restrict__ dst, int64_t n, uint64_t seed, float std) {
+  const int64_t npair = (n + 1) >> 1;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < npair;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t h = splitmix64(seed ^ splitmix64(static_cast<uint64_t>(i)));
+    const float u1 = (static_cast<float>(h >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
+    const float u2 = static_cast<float>((h >> 16) & 0xFFFFFFull) * (1.0f / 16777216.0f);
+    const float r = sqrtf(-2.0f * logf(u1)) * std;
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    dst[2 * i] = r * cs;
+    if (2 * i + 1 < n) dst[2 * i + 1] = r * sn;
+  }
+}
+__global__ void nonfinite_kernel(const float* __restrict__ x, int64_t n, int* flag) {
+  bool bad = false;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    bad |= !isfinite(x[i]);
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicExch(flag, 1);
+}
+
+int grid_for(int64_t work, int threads) {
+  const int64_t b = (work + threads - 1) / threads;
+  const int64_t cap = 148 * 16;
+  return static_cast<int>(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+}  // namespace
+
+int embed_gather(const float* E, const uint32_t* tok, float* x, int M, int D, int V, int* err, cudaStream_t s) {
+  if (D % 4) return -1;
+  embed_gather_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(E, tok, x, M, D, V, err);
+  return cudaGetLastError();
+}
+int embed_scatter(const float* dx, const int32_t* perm, const int32_t* seg_start, const uint32_t* seg_tok, int nseg,
+                  float* dE, int D, cudaStream_t s) {
+  if (D % 4) return -1;
+  if (nseg == 0) return 0;
+  embed_scatter_kernel<<<nseg, 256, 0, s>>>(dx, perm, seg_start, seg_tok, dE, D);
+  return cudaGetLastError();
+}
+int rmsnorm_fwd(const float* x, const float* gamma, __nv_bfloat16* out, float* rms_inv, int M, int D, cudaStream_t s) {
+  if (D % 4) return -1;
+  rmsnorm_fwd_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, gamma, out, rms_inv, M, D);
+  return cudaGetLastError();
+}
+int rmsnorm_bwd_blocks(int M) { return (M + kBwdRows - 1) / kBwdRows; }
+int rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float* rms_inv, const float* resid,
+                float* dx, __nv_bfloat16* dx_bf16, float bf16_scale, float* dgamma_part, int M, int D,
+                cudaStream_t s) {
+  if (D % 4 || D > 4 * kBwdThreads * kBwdVec) return -1;
+  rmsnorm_bwd_kernel<<<rmsnorm_bwd_blocks(M), kBwdThreads, 0, s>>>(dy, x, gamma, rms_inv, resid, dx, dx_bf16,
+                                                                   bf16_scale, dgamma_part, M, D);
+  return cudaGetLastError();
+}
+int dgamma_reduce(const float* part, int nblk, float* dgamma, int D, int accumulate, cudaStream_t s) {
+  dgamma_reduce_kernel<<<(D + 255) / 256, 256, 0, s>>>(part, nblk, dgamma, D, accumulate);
+  return cudaGetLastError();
+}
+int ce_forward(const float* logits, const uint32_t* tgt, float* row_loss, float* row_lse, int M, int V,
+               float softcap, cudaStream_t s) {
+  if (V % 4 || V > 4 * kCeThreads * kCeVec) return -1;
+  ce_forward_kernel<<<M, kCeThreads, 0, s>>>(logits, tgt, row_loss, row_lse, V, softcap);
+  return cudaGetLastError();
+}
+int ce_backward(const float* logits, const float* row_lse, const uint32_t* tgt, __nv_bfloat16* dl, int M, int V,
+                float softcap, float scale, cudaStream_t s) {
+  if (V % 4) return -1;
+  ce_backward_kernel<<<M, kCeThreads, 0, s>>>(logits, row_lse, tgt, dl, V, softcap, scale);
+  return cudaGetLastError();
+}
+int mean_reduce(const float* row_loss, int M, float* out, cudaStream_t s) {
+  mean_reduce_kernel<<<1, 1024, 0, s>>>(row_loss, M, out);
+  return cudaGetLastError();
+}
+int sumsq_partials_count() { return kNormBlocks; }
+int sumsq_norm(const float* x, int64_t n, float* partials, float* out_norm, cudaStream_t s) {
+  sumsq_partial_kernel<<<kNormBlocks, kNormThreads, 0, s>>>(x, n, partials);
+  sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, kNormBlocks, out_norm);
+  return cudaGetLastError();
+}
+int adam_step(const AdamArgs& a, cudaStream_t s) {
+  AdamKParams k;
+  for (int i = 0; i < 4; ++i) k.seg[i] = a.seg[i];
+  k.nseg = a.nseg;
+  int64_t total = 0;
+  for (int i = 0; i < a.nseg; ++i) {
+    if (a.seg[i].begin % 4 || a.seg[i].end % 4) return -1;
+    total += a.seg[i].end - a.seg[i].begin;
+  }
+  k.beta1 = a.beta1;
+  k.beta2 = a.beta2;
+  k.eps = a.eps;
+  k.bc1 = a.bc1;
+  k.bc2 = a.bc2;
+  k.grad_scale = a.grad_scale;
+  k.gsc = a.gsc;
+  k.clip = a.clip;
+  adam_kernel<<<grid_for(total / 4, 256), 256, 0, s>>>(a.param, a.grad, a.m, a.v, a.param_bf16, a.norm, k);
+  return cudaGetLastError();
+}
+int cast_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s) {
+  if (n % 4) return -1;
+  cast_bf16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(src, dst, n / 4);
+  return cudaGetLastError();
+}
+int fill_f32(float* dst, int64_t n, float value, cudaStream_t s) {
+  fill_kernel<<<grid_for(n, 256), 256, 0, s>>>(dst, n, value);
+  return cudaGetLastError();
+}
+int init_normal(float* dst, int64_t n, uint64_t seed, float std, cudaStream_t s) {
+  init_normal_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(dst, n, seed, std);
+  return cudaGetLastError();
+}
+int scale_f32(const float* x, float* y, int64_t n, float a, cudaStream_t s) {
+  scale_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n, a);
+  return cudaGetLastError();
+}
+int nonfinite_check(const float* x, int64_t n, int* flag, cudaStream_t s) {
+  nonfinite_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, flag);
+  return cudaGetLastError();
+}
+
+}  // namespace rt

@@ -1,0 +1,1160 @@
+// Model-level C ABI of librustane_cuda: context, device arenas, host<->device
+// transfers and the orchestration of forward, backward and AdamW.
+//
+// The orchestration restates the reference engine in token-major form:
+//   full_model::forward_ws  (crates/engine/src/full_model.rs:187-247)
+//   layer::forward_into     (crates/engine/src/layer.rs:552-680)
+//   full_model::backward_ws (full_model.rs:250-331)
+//   layer::backward_into    (layer.rs:1606-1858)
+//   full_model::update_weights / grad_norm / train_step (full_model.rs:490-714)
+// Every heavy step runs in one of the sm_100a kernels (gemm.cu, attention.cu,
+// elementwise.cu); there is no CPU compute path.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <thread>
+
+#include "attention.h"
+#include "common.cuh"
+#include "elementwise.h"
+#include "kernels.h"
+#include "runtime.h"
+
+using rt::bf16;
+
+// ================================================================ NCCL (dlopen)
+namespace rt {
+struct NcclApi {
+  void* handle = nullptr;
+  decltype(&ncclGetUniqueId) getUniqueId = nullptr;
+  decltype(&ncclCommInitRank) commInitRank = nullptr;
+  decltype(&ncclAllReduce) allReduce = nullptr;
+  decltype(&ncclCommGetAsyncError) getAsyncError = nullptr;
+  decltype(&ncclCommAbort) commAbort = nullptr;
+  decltype(&ncclCommDestroy) commDestroy = nullptr;
+  decltype(&ncclGetErrorString) errorString = nullptr;
+};
+struct NcclState {
+  ncclComm_t comm = nullptr;
+  bool aborted = false;
+};
+
+static NcclApi* nccl_api() {
+  static NcclApi api;
+  static bool tried = false;
+  if (tried) return api.handle ? &api : nullptr;
+  tried = true;
+  const char* env = getenv("RUSTANE_NCCL_LIB");
+  void* h = nullptr;
+  if (env && *env) h = dlopen(env, RTLD_NOW | RTLD_GLOBAL);
+  if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD | RTLD_GLOBAL);  // already loaded (e.g. by torch)
+  if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) return nullptr;
+  api.handle = h;
+#define RT_SYM(field, name) api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name))
+  RT_SYM(getUniqueId, "ncclGetUniqueId");
+  RT_SYM(commInitRank, "ncclCommInitRank");
+  RT_SYM(allReduce, "ncclAllReduce");
+  RT_SYM(getAsyncError, "ncclCommGetAsyncError");
+  RT_SYM(commAbort, "ncclCommAbort");
+  RT_SYM(commDestroy, "ncclCommDestroy");
+  RT_SYM(errorString, "ncclGetErrorString");
+#undef RT_SYM
+  if (!api.getUniqueId || !api.commInitRank || !api.allReduce || !api.getAsyncError || !api.commAbort ||
+      !api.commDestroy) {
+    api.handle = nullptr;
+    return nullptr;
+  }
+  return &api;
+}
+}  // namespace rt
+
+// ================================================================ helpers
+namespace {
+
+int set_err(rt_ctx* c, int code, const std::string& msg) {
+  if (c) c->last_error = msg;
+  return code;
+}
+
+int cuda_err(rt_ctx* c, cudaError_t e, const char* what) {
+  return set_err(c, RT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define RT_CUDA(call, what)                        \
+  do {                                             \
+    cudaError_t _e = (call);                       \
+    if (_e != cudaSuccess) return cuda_err(c, _e, what); \
+  } while (0)
+
+#define RT_LAUNCH(call, what)                                                                     \
+  do {                                                                                            \
+    int _rc = (call);                                                                             \
+    if (_rc != 0)                                                                                 \
+      return set_err(c, _rc == -1 ? RT_ERR_SHAPE : RT_ERR_CUDA,                                   \
+                     std::string(what) + " launch failed (" + std::to_string(_rc) + ")");         \
+  } while (0)
+
+template <class T>
+T* dalloc(rt_ctx* c, int64_t count) {
+  if (count <= 0) return nullptr;
+  size_t bytes = (static_cast<size_t>(count) * sizeof(T) + 255) & ~size_t(255);
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+  c->allocations.push_back(p);
+  c->device_bytes += static_cast<int64_t>(bytes);
+  return static_cast<T*>(p);
+}
+
+cudaEvent_t pool_event(rt_ctx* c) {
+  if (c->event_pool_used == c->event_pool.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    c->event_pool.push_back(e);
+  }
+  return c->event_pool[c->event_pool_used++];
+}
+
+// Run one launcher, count its kernels and time it when profiling.
+template <class F>
+int launch(rt_ctx* c, int kind, double flops, int nkernels, F&& f) {
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (c->profiling) {
+    a = pool_event(c);
+    cudaEventRecord(a, c->stream);
+  }
+  const int rc = f();
+  if (c->profiling) {
+    b = pool_event(c);
+    cudaEventRecord(b, c->stream);
+    c->kevents.push_back({kind, flops, a, b});
+  }
+  c->acc.kernel_launches += nkernels;
+  if (kind == 0) c->acc.gemm_launches += nkernels;
+  else if (kind == 1) c->acc.attn_launches += nkernels;
+  else c->acc.other_launches += nkernels;
+  return rc;
+}
+
+void harvest_kernel_events(rt_ctx* c) {
+  for (const auto& k : c->kevents) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, k.a, k.b) != cudaSuccess) continue;
+    if (k.kind == 0) {
+      c->acc.gemm_ms += ms;
+      c->acc.gemm_flops += k.flops;
+    } else if (k.kind == 1) {
+      c->acc.attn_ms += ms;
+      c->acc.attn_flops += k.flops;
+    } else {
+      c->acc.other_ms += ms;
+    }
+  }
+  c->kevents.clear();
+  c->event_pool_used = 0;
+}
+
+int gemm(rt_ctx* c, rt::GemmArgs g, const char* what) {
+  g.err = c->d_err;
+  const double n_out = g.epi == rt::kEpiSwiglu ? 2.0 * g.N : double(g.N);
+  const double fl = 2.0 * double(g.M) * n_out * double(g.K);
+  RT_LAUNCH(launch(c, 0, fl, 1, [&] { return rt::gemm_launch(g, c->stream); }), what);
+  return RT_OK;
+}
+
+int other(rt_ctx* c, int nk, int rc_in, const char* what) {
+  (void)nk;
+  if (rc_in != 0)
+    return set_err(c, rc_in == -1 ? RT_ERR_SHAPE : RT_ERR_CUDA,
+                   std::string(what) + " launch failed (" + std::to_string(rc_in) + ")");
+  return RT_OK;
+}
+
+#define RT_OTHER(nk, expr, what) \
+  do {                           \
+    int _r = launch(c, 2, 0.0, nk, [&] { return (expr); }); \
+    if (_r != 0) return other(c, nk, _r, what); \
+  } while (0)
+
+bool forward_only(const rt_ctx* c) { return (c->flags & RT_CTX_FORWARD_ONLY) != 0; }
+float alpha_of(const rt_model_config& cfg) { return 1.0f / std::sqrt(2.0f * static_cast<float>(cfg.nlayers)); }
+
+// Gamma pointers: training arenas keep them after the matrices; forward-only
+// contexts keep [embed | gammas] in a compact fp32 buffer.
+float* gamma_base(rt_ctx* c) { return c->params + (forward_only(c) ? c->n_embed : c->n_matrix_end); }
+
+// Wait for the stream; with a communicator, poll so that a stuck collective
+// aborts after timeout_ms instead of blocking forever.
+int wait_stream(rt_ctx* c) {
+  if (!c->nccl || !c->nccl->comm) {
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_err(c, e, "stream synchronize");
+  } else {
+    rt::NcclApi* api = rt::nccl_api();
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+      cudaError_t q = cudaStreamQuery(c->stream);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) return cuda_err(c, q, "stream query");
+      ncclResult_t ar = ncclSuccess;
+      api->getAsyncError(c->nccl->comm, &ar);
+      const auto ms =
+          std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+      if ((ar != ncclSuccess && ar != ncclInProgress) || (c->timeout_ms > 0 && ms > c->timeout_ms)) {
+        api->commAbort(c->nccl->comm);
+        c->nccl->comm = nullptr;
+        c->nccl->aborted = true;
+        return set_err(c, RT_ERR_NCCL, ar != ncclSuccess ? std::string("NCCL async error: ") + api->errorString(ar)
+                                                         : "NCCL collective timed out; communicator aborted");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+  }
+  int herr = 0;
+  cudaError_t e = cudaMemcpy(&herr, c->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_err(c, e, "read device error word");
+  if (herr != 0) {
+    cudaMemset(c->d_err, 0, sizeof(int));
+    return set_err(c, herr == rt::kDevBadToken ? RT_ERR_TOKEN : RT_ERR_DEVICE,
+                   "device error code " + std::to_string(herr) +
+                       (herr <= 3 ? " (pipeline wait timed out)" : herr == 4 ? " (token id out of range)" : ""));
+  }
+  if (c->profiling) harvest_kernel_events(c);
+  return RT_OK;
+}
+
+void compute_rope_tables(const rt_model_config& cfg, std::vector<float>& cf, std::vector<float>& sf,
+                         std::vector<float>& cb, std::vector<float>& sb) {
+  const int S = cfg.seq, hd = cfg.hd, pairs = hd / 2;
+  cf.assign(size_t(S) * pairs, 0.f);
+  sf.assign(size_t(S) * pairs, 0.f);
+  cb.assign(size_t(pairs) * S, 0.f);
+  sb.assign(size_t(pairs) * S, 0.f);
+  for (int p = 0; p < S; ++p)
+    for (int i = 0; i < pairs; ++i) {  // kernels/sdpa_fwd.rs:18-33
+      const float theta = static_cast<float>(p) / powf(10000.0f, 2.0f * static_cast<float>(i) / static_cast<float>(hd));
+      cf[size_t(p) * pairs + i] = cosf(theta);
+      sf[size_t(p) * pairs + i] = sinf(theta);
+    }
+  for (int i = 0; i < pairs; ++i) {  // layer.rs:203-216
+    const float freq = 1.0f / powf(10000.0f, 2.0f * static_cast<float>(i) / static_cast<float>(hd));
+    for (int p = 0; p < S; ++p) {
+      const float theta = static_cast<float>(p) * freq;
+      cb[size_t(i) * S + p] = cosf(theta);
+      sb[size_t(i) * S + p] = sinf(theta);
+    }
+  }
+}
+
+// ------------------------------------------------------------ host copies
+// Copy a [rows, cols] host matrix into columns [col0, col0+cols) of a device
+// matrix with row stride ld (elements), or back.
+int copy_block_h2d(rt_ctx* c, float* dst, int64_t ld, int64_t col0, const float* src, int64_t rows, int64_t cols) {
+  RT_CUDA(cudaMemcpy2D(dst + col0, ld * sizeof(float), src, cols * sizeof(float), cols * sizeof(float), rows,
+                       cudaMemcpyHostToDevice),
+          "upload");
+  return RT_OK;
+}
+int copy_block_d2h(rt_ctx* c, float* dst, const float* src, int64_t ld, int64_t col0, int64_t rows, int64_t cols) {
+  RT_CUDA(cudaMemcpy2D(dst, cols * sizeof(float), src + col0, ld * sizeof(float), cols * sizeof(float), rows,
+                       cudaMemcpyDeviceToHost),
+          "download");
+  return RT_OK;
+}
+
+// Host tensors <-> one fp32 arena laid out like the parameters.
+int arena_h2d(rt_ctx* c, float* arena, const rt_model_ptrs* h) {
+  const auto& cfg = c->cfg;
+  const int64_t D = cfg.dim, H = cfg.hidden, Q = cfg.q_dim;
+  if (!h || !h->embed || !h->gamma_final || !h->layers) return set_err(c, RT_ERR_ARG, "null model pointers");
+  RT_CUDA(cudaMemcpy(arena, h->embed, sizeof(float) * cfg.vocab * D, cudaMemcpyHostToDevice), "upload embed");
+  float* gb = arena + c->n_matrix_end;
+  RT_CUDA(cudaMemcpy(gb, h->gamma_final, sizeof(float) * D, cudaMemcpyHostToDevice), "upload gamma_final");
+  for (int l = 0; l < cfg.nlayers; ++l) {
+    const rt_layer_ptrs& L = h->layers[l];
+    const auto& o = c->layer_off[l];
+    if (!L.wq || !L.wk || !L.wv || !L.wo || !L.w1 || !L.w3 || !L.w2 || !L.gamma1 || !L.gamma2)
+      return set_err(c, RT_ERR_ARG, "null layer pointer");
+    int rc;
+    if ((rc = copy_block_h2d(c, arena + o.wqkv, 3 * D, 0, L.wq, D, D))) return rc;
+    if ((rc = copy_block_h2d(c, arena + o.wqkv, 3 * D, D, L.wk, D, D))) return rc;
+    if ((rc = copy_block_h2d(c, arena + o.wqkv, 3 * D, 2 * D, L.wv, D, D))) return rc;
+    RT_CUDA(cudaMemcpy(arena + o.wo, L.wo, sizeof(float) * Q * D, cudaMemcpyHostToDevice), "upload wo");
+    if ((rc = copy_block_h2d(c, arena + o.w13, 2 * H, 0, L.w1, D, H))) return rc;
+    if ((rc = copy_block_h2d(c, arena + o.w13, 2 * H, H, L.w3, D, H))) return rc;
+    RT_CUDA(cudaMemcpy(arena + o.w2, L.w2, sizeof(float) * D * H, cudaMemcpyHostToDevice), "upload w2");
+    RT_CUDA(cudaMemcpy(arena + o.gamma1, L.gamma1, sizeof(float) * D, cudaMemcpyHostToDevice), "upload gamma1");
+    RT_CUDA(cudaMemcpy(arena + o.gamma2, L.gamma2, sizeof(float) * D, cudaMemcpyHostToDevice), "upload gamma2");
+  }
+  return RT_OK;
+}
+
+int arena_d2h(rt_ctx* c, const float* arena, const rt_model_ptrs* h) {
+  const auto& cfg = c->cfg;
+  const int64_t D = cfg.dim, H = cfg.hidden, Q = cfg.q_dim;
+  if (!h || !h->embed || !h->gamma_final || !h->layers) return set_err(c, RT_ERR_ARG, "null model pointers");
+  RT_CUDA(cudaMemcpy(h->embed, arena, sizeof(float) * cfg.vocab * D, cudaMemcpyDeviceToHost), "download embed");
+  RT_CUDA(cudaMemcpy(h->gamma_final, arena + c->n_matrix_end, sizeof(float) * D, cudaMemcpyDeviceToHost),
+          "download gamma_final");
+  for (int l = 0; l < cfg.nlayers; ++l) {
+    const rt_layer_ptrs& L = h->layers[l];
+    const auto& o = c->layer_off[l];
+    int rc;
+    if ((rc = copy_block_d2h(c, L.wq, arena + o.wqkv, 3 * D, 0, D, D))) return rc;
+    if ((rc = copy_block_d2h(c, L.wk, arena + o.wqkv, 3 * D, D, D, D))) return rc;
+    if ((rc = copy_block_d2h(c, L.wv, arena + o.wqkv, 3 * D, 2 * D, D, D))) return rc;
+    RT_CUDA(cudaMemcpy(L.wo, arena + o.wo, sizeof(float) * Q * D, cudaMemcpyDeviceToHost), "download wo");
+    if ((rc = copy_block_d2h(c, L.w1, arena + o.w13, 2 * H, 0, D, H))) return rc;
+    if ((rc = copy_block_d2h(c, L.w3, arena + o.w13, 2 * H, H, D, H))) return rc;
+    RT_CUDA(cudaMemcpy(L.w2, arena + o.w2, sizeof(float) * D * H, cudaMemcpyDeviceToHost), "download w2");
+    RT_CUDA(cudaMemcpy(L.gamma1, arena + o.gamma1, sizeof(float) * D, cudaMemcpyDeviceToHost), "download gamma1");
+    RT_CUDA(cudaMemcpy(L.gamma2, arena + o.gamma2, sizeof(float) * D, cudaMemcpyDeviceToHost), "download gamma2");
+  }
+  return RT_OK;
+}
+
+int materialize_zero_grads(rt_ctx* c) {
+  if (c->grads_zero_pending) {
+    RT_CUDA(cudaMemsetAsync(c->grads, 0, sizeof(float) * c->n_params, c->stream), "zero grads");
+    c->grads_zero_pending = false;
+  }
+  return RT_OK;
+}
+
+// Tokens -> device, with the embedding-scatter segments built on the host
+// (counting sort by token, positions ascending within a token).
+int upload_tokens(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets, int batch) {
+  const int M = batch * c->cfg.seq;
+  const uint32_t V = static_cast<uint32_t>(c->cfg.vocab);
+  for (int i = 0; i < M; ++i)
+    if (tokens[i] >= V || (targets && targets[i] >= V))
+      return set_err(c, RT_ERR_TOKEN, "token id " + std::to_string(tokens[i] >= V ? tokens[i] : targets[i]) +
+                                          " at position " + std::to_string(i) + " >= vocab " + std::to_string(V));
+  uint32_t* st_tok = static_cast<uint32_t*>(c->h_stage);
+  uint32_t* st_tgt = st_tok + M;
+  int32_t* st_perm = reinterpret_cast<int32_t*>(st_tgt + M);
+  int32_t* st_start = st_perm + M;
+  uint32_t* st_segtok = reinterpret_cast<uint32_t*>(st_start + M + 1);
+  memcpy(st_tok, tokens, sizeof(uint32_t) * M);
+  if (targets) memcpy(st_tgt, targets, sizeof(uint32_t) * M);
+  std::vector<int32_t> count(V + 1, 0);
+  for (int i = 0; i < M; ++i) count[tokens[i] + 1]++;
+  for (uint32_t v = 0; v < V; ++v) count[v + 1] += count[v];
+  int nseg = 0;
+  for (uint32_t v = 0; v < V; ++v)
+    if (count[v + 1] > count[v]) {
+      st_start[nseg] = count[v];
+      st_segtok[nseg] = v;
+      ++nseg;
+    }
+  st_start[nseg] = M;
+  std::vector<int32_t> fillpos(count.begin(), count.end() - 1);
+  for (int i = 0; i < M; ++i) st_perm[fillpos[tokens[i]]++] = i;
+  c->nseg = nseg;
+  RT_CUDA(cudaMemcpyAsync(c->d_tokens, st_tok, sizeof(uint32_t) * M, cudaMemcpyHostToDevice, c->stream), "tokens");
+  if (targets)
+    RT_CUDA(cudaMemcpyAsync(c->d_targets, st_tgt, sizeof(uint32_t) * M, cudaMemcpyHostToDevice, c->stream),
+            "targets");
+  RT_CUDA(cudaMemcpyAsync(c->d_perm, st_perm, sizeof(int32_t) * M, cudaMemcpyHostToDevice, c->stream), "perm");
+  RT_CUDA(cudaMemcpyAsync(c->d_seg_start, st_start, sizeof(int32_t) * (nseg + 1), cudaMemcpyHostToDevice, c->stream),
+          "seg_start");
+  RT_CUDA(cudaMemcpyAsync(c->d_seg_tok, st_segtok, sizeof(uint32_t) * nseg, cudaMemcpyHostToDevice, c->stream),
+          "seg_tok");
+  return RT_OK;
+}
+
+// ---------------------------------------------------------------- forward
+int layer_forward(rt_ctx* c, int l, const rt::LayerActs& A, const float* x_in, float* x_next, int batch) {
+  const auto& cfg = c->cfg;
+  const int D = cfg.dim, H = cfg.hidden, S = cfg.seq, M = batch * S;
+  const float alpha = alpha_of(cfg);
+  const auto& o = c->layer_off[l];
+  const bf16* W = c->params_bf16;
+  const float* G = gamma_base(c);
+  const int64_t goff = c->n_matrix_end;  // gamma offsets are relative to gamma_base()
+  int rc;
+  RT_OTHER(1, rt::rmsnorm_fwd(x_in, G + (o.gamma1 - goff), A.xn, A.rms1, M, D, c->stream), "rmsnorm1");
+  {  // Q K V projection + RoPE (sdpaFwd, kernels/sdpa_fwd.rs:80-128)
+    rt::GemmArgs g;
+    g.a = A.xn; g.lda = D;
+    g.b = W + o.wqkv; g.ldb = 3 * D; g.b_mn = true;
+    g.M = M; g.N = 3 * D; g.K = D;
+    g.epi = rt::kEpiRope; g.out = A.qkv; g.ldo = 3 * D;
+    g.rope_cos = c->rope_cos_f; g.rope_sin = c->rope_sin_f; g.seq = S; g.rope_cols = 2 * D;
+    if ((rc = gemm(c, g, "qkv"))) return rc;
+  }
+  {  // causal attention (sdpa_fwd.rs:130-150)
+    rt::AttnArgs a;
+    a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
+    a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
+    const double fl = 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
+    RT_LAUNCH(launch(c, 1, fl, 1, [&] { return rt::attn_forward(a, c->stream); }), "attention fwd");
+  }
+  {  // woFwd + residual x2 = x + alpha * o (layer.rs:769-784)
+    rt::GemmArgs g;
+    g.a = A.attn; g.lda = D;
+    g.b = W + o.wo; g.ldb = D; g.b_mn = true;
+    g.M = M; g.N = D; g.K = cfg.q_dim;
+    g.epi = rt::kEpiResidual; g.aux = x_in; g.ld_aux = D; g.out = A.x2; g.ldo = D; g.alpha = alpha;
+    if ((rc = gemm(c, g, "wo"))) return rc;
+  }
+  RT_OTHER(1, rt::rmsnorm_fwd(A.x2, G + (o.gamma2 - goff), A.x2n, A.rms2, M, D, c->stream), "rmsnorm2");
+  {  // W1 | W3 + SwiGLU (ffn_fused.rs:46-63)
+    rt::GemmArgs g;
+    g.a = A.x2n; g.lda = D;
+    g.b = W + o.w13; g.ldb = 2 * H; g.b_mn = true;
+    g.M = M; g.N = H; g.K = D;
+    g.epi = rt::kEpiSwiglu; g.out = A.h13; g.ldo = 2 * H; g.out2 = A.gate; g.ldo2 = H; g.n_half = H;
+    if ((rc = gemm(c, g, "w13"))) return rc;
+  }
+  {  // gate W2^T + residual (ffn_fused.rs:65-78)
+    rt::GemmArgs g;
+    g.a = A.gate; g.lda = H;
+    g.b = W + o.w2; g.ldb = H; g.b_mn = false;
+    g.M = M; g.N = D; g.K = H;
+    g.epi = rt::kEpiResidual; g.aux = A.x2; g.ld_aux = D; g.out = x_next; g.ldo = D; g.alpha = alpha;
+    if ((rc = gemm(c, g, "w2"))) return rc;
+  }
+  return RT_OK;
+}
+
+int forward_impl(rt_ctx* c, int batch, float softcap) {
+  const auto& cfg = c->cfg;
+  const int D = cfg.dim, V = cfg.vocab, M = batch * cfg.seq;
+  int rc;
+  cudaEventRecord(c->ev[0], c->stream);
+  float* x0 = c->acts[0].x;
+  RT_OTHER(1, rt::embed_gather(c->params, c->d_tokens, x0, M, D, V, c->d_err, c->stream), "embed gather");
+  float* x = x0;
+  for (int l = 0; l < cfg.nlayers; ++l) {
+    const rt::LayerActs& A = forward_only(c) ? c->acts[0] : c->acts[l];
+    float* x_next;
+    if (forward_only(c))
+      x_next = (l + 1 == cfg.nlayers) ? c->x_out : (x == c->acts[0].x ? c->dy_a : c->acts[0].x);
+    else
+      x_next = (l + 1 == cfg.nlayers) ? c->x_out : c->acts[l + 1].x;
+    if ((rc = layer_forward(c, l, A, x, x_next, batch))) return rc;
+    x = x_next;
+  }
+  const float* gf = gamma_base(c);  // gamma_final sits first among the gammas
+  RT_OTHER(1, rt::rmsnorm_fwd(c->x_out, gf, c->xf, c->rms_f, M, D, c->stream), "final rmsnorm");
+  {  // tied-embedding logits (full_model.rs:228-230)
+    rt::GemmArgs g;
+    g.a = c->xf; g.lda = D;
+    g.b = c->params_bf16; g.ldb = D; g.b_mn = false;
+    g.M = M; g.N = V; g.K = D;
+    g.epi = rt::kEpiF32; g.out = c->logits; g.ldo = V;
+    if ((rc = gemm(c, g, "logits"))) return rc;
+  }
+  RT_OTHER(1, rt::ce_forward(c->logits, c->d_targets, c->row_loss, c->row_lse, M, V, softcap, c->stream), "ce fwd");
+  RT_OTHER(1, rt::mean_reduce(c->row_loss, M, c->d_loss, c->stream), "loss mean");
+  cudaEventRecord(c->ev[1], c->stream);
+  c->cur_batch = batch;
+  c->fwd_done = true;
+  c->last_softcap = softcap;
+  return RT_OK;
+}
+
+// --------------------------------------------------------------- backward
+int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
+  const auto& cfg = c->cfg;
+  const int D = cfg.dim, H = cfg.hidden, V = cfg.vocab, S = cfg.seq;
+  const int batch = c->cur_batch, M = batch * S;
+  const float alpha = alpha_of(cfg);
+  const int beta = c->grads_zero_pending ? 0 : 1;
+  const bf16* W = c->params_bf16;
+  const float* P = c->params;
+  float* Gr = c->grads;
+  const int nblk = rt::rmsnorm_bwd_blocks(M);
+  int rc;
+  cudaEventRecord(c->ev[2], c->stream);
+  // dlogits * loss_scale (full_model.rs:265-276); CE mean over seq per sequence (cross_entropy.rs:92-95)
+  RT_OTHER(1, rt::ce_backward(c->logits, c->row_lse, c->d_targets, c->dl, M, V, softcap, loss_scale / S, c->stream),
+           "ce bwd");
+  {  // dx_final = dl * E   (full_model.rs:279-289)
+    rt::GemmArgs g;
+    g.a = c->dl; g.lda = V;
+    g.b = W; g.ldb = D; g.b_mn = true;
+    g.M = M; g.N = D; g.K = V;
+    g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
+    if ((rc = gemm(c, g, "dx_final"))) return rc;
+  }
+  {  // dE += dl^T x_final   (full_model.rs:299-312)
+    rt::GemmArgs g;
+    g.a = c->dl; g.lda = V; g.a_mn = true;
+    g.b = c->xf; g.ldb = D; g.b_mn = true;
+    g.M = V; g.N = D; g.K = M;
+    g.epi = rt::kEpiF32Acc; g.out = Gr; g.ldo = D; g.beta = beta;
+    if ((rc = gemm(c, g, "dE"))) return rc;
+  }
+  // final RMSNorm backward (full_model.rs:315-318); also alpha*dy for the last layer
+  RT_OTHER(1, rt::rmsnorm_bwd(c->dx_tmp, c->x_out, P + c->off_gamma_final, c->rms_f, nullptr, c->dy_a, c->dffn, alpha,
+                              c->dgamma_part, M, D, c->stream),
+           "final rmsnorm bwd");
+  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + c->off_gamma_final, D, beta, c->stream), "dgamma");
+  float* dy = c->dy_a;
+  float* dy_next = c->dy_b;
+  for (int l = cfg.nlayers - 1; l >= 0; --l) {
+    const rt::LayerActs& A = c->acts[l];
+    const auto& o = c->layer_off[l];
+    {  // ffnBwdW2t + SiLU backward (layer.rs:1627-1667)
+      rt::GemmArgs g;
+      g.a = c->dffn; g.lda = D;
+      g.b = W + o.w2; g.ldb = H; g.b_mn = true;
+      g.M = M; g.N = H; g.K = D;
+      g.epi = rt::kEpiSwigluBwd; g.aux = A.h13; g.ld_aux = 2 * H; g.out = c->dh13; g.ldo = 2 * H; g.n_half = H;
+      if ((rc = gemm(c, g, "dgate"))) return rc;
+    }
+    {  // dW2 += dffn^T gate (layer.rs:1754)
+      rt::GemmArgs g;
+      g.a = c->dffn; g.lda = D; g.a_mn = true;
+      g.b = A.gate; g.ldb = H; g.b_mn = true;
+      g.M = D; g.N = H; g.K = M;
+      g.epi = rt::kEpiF32Acc; g.out = Gr + o.w2; g.ldo = H; g.beta = beta;
+      if ((rc = gemm(c, g, "dW2"))) return rc;
+    }
+    {  // ffnBwdW13t: dx_ffn = dh1 W1^T + dh3 W3^T (layer.rs:1671-1699)
+      rt::GemmArgs g;
+      g.a = c->dh13; g.lda = 2 * H;
+      g.b = W + o.w13; g.ldb = 2 * H; g.b_mn = false;
+      g.M = M; g.N = D; g.K = 2 * H;
+      g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
+      if ((rc = gemm(c, g, "dx_ffn"))) return rc;
+    }
+    {  // dW1 | dW3 += x2norm^T (dh1 | dh3) (layer.rs:1692, 1787)
+      rt::GemmArgs g;
+      g.a = A.x2n; g.lda = D; g.a_mn = true;
+      g.b = c->dh13; g.ldb = 2 * H; g.b_mn = true;
+      g.M = D; g.N = 2 * H; g.K = M;
+      g.epi = rt::kEpiF32Acc; g.out = Gr + o.w13; g.ldo = 2 * H; g.beta = beta;
+      if ((rc = gemm(c, g, "dW13"))) return rc;
+    }
+    // RMSNorm2 backward + dy (layer.rs:1702-1706); dx2s = alpha * dx2
+    RT_OTHER(1, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s, alpha, c->dgamma_part, M,
+                                D, c->stream),
+             "rmsnorm2 bwd");
+    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma2, D, beta, c->stream), "dgamma2");
+    {  // wotBwd: da = dx2s Wo^T (layer.rs:1709-1733)
+      rt::GemmArgs g;
+      g.a = c->dx2s; g.lda = D;
+      g.b = W + o.wo; g.ldb = D; g.b_mn = false;
+      g.M = M; g.N = cfg.q_dim; g.K = D;
+      g.epi = rt::kEpiBf16; g.out = c->da; g.ldo = cfg.q_dim;
+      if ((rc = gemm(c, g, "da"))) return rc;
+    }
+    {  // dWo += attn^T dx2s (layer.rs:1753)
+      rt::GemmArgs g;
+      g.a = A.attn; g.lda = cfg.q_dim; g.a_mn = true;
+      g.b = c->dx2s; g.ldb = D; g.b_mn = true;
+      g.M = cfg.q_dim; g.N = D; g.K = M;
+      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wo; g.ldo = D; g.beta = beta;
+      if ((rc = gemm(c, g, "dWo"))) return rc;
+    }
+    {  // sdpaBwd1 + sdpaBwd2 + RoPE backward (layer.rs:1736-1798)
+      rt::AttnArgs a;
+      a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
+      a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
+      a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv; a.lddq = 3 * D;
+      a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b;
+      const double fl = 2.5 * 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
+      RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward(a, c->stream); }), "attention bwd");
+    }
+    {  // qBwd + kvBwd: dx_attn = dq Wq^T + dk Wk^T + dv Wv^T (layer.rs:1800-1850)
+      rt::GemmArgs g;
+      g.a = c->dqkv; g.lda = 3 * D;
+      g.b = W + o.wqkv; g.ldb = 3 * D; g.b_mn = false;
+      g.M = M; g.N = D; g.K = 3 * D;
+      g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
+      if ((rc = gemm(c, g, "dx_attn"))) return rc;
+    }
+    {  // dWq | dWk | dWv += xnorm^T (dq | dk | dv) (layer.rs:1838-1840)
+      rt::GemmArgs g;
+      g.a = A.xn; g.lda = D; g.a_mn = true;
+      g.b = c->dqkv; g.ldb = 3 * D; g.b_mn = true;
+      g.M = D; g.N = 3 * D; g.K = M;
+      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wqkv; g.ldo = 3 * D; g.beta = beta;
+      if ((rc = gemm(c, g, "dWqkv"))) return rc;
+    }
+    // RMSNorm1 backward + dx2 (layer.rs:1853-1857); alpha * dx for the layer below
+    RT_OTHER(1, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next, l > 0 ? c->dffn : nullptr,
+                                alpha, c->dgamma_part, M, D, c->stream),
+             "rmsnorm1 bwd");
+    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma1, D, beta, c->stream), "dgamma1");
+    std::swap(dy, dy_next);
+  }
+  // embedding scatter-add (full_model.rs:330)
+  RT_OTHER(1, rt::embed_scatter(dy, c->d_perm, c->d_seg_start, c->d_seg_tok, c->nseg, Gr, D, c->stream),
+           "embed scatter");
+  cudaEventRecord(c->ev[3], c->stream);
+  c->grads_zero_pending = false;
+  return RT_OK;
+}
+
+float powi_f32(float b, uint32_t t) {
+  float r = 1.f;
+  for (uint32_t i = 0; i < t; ++i) r *= b;
+  return r;
+}
+
+int adam_impl(rt_ctx* c, uint32_t t, float lr, const rt_train_config* tc, float grad_scale, const float* d_norm,
+              float gsc, float clip) {
+  rt::AdamArgs a;
+  a.param = c->params;
+  a.grad = c->grads;
+  a.m = c->mom1;
+  a.v = c->mom2;
+  a.param_bf16 = c->params_bf16;
+  a.nseg = 3;
+  a.seg[0] = {0, c->n_embed, lr * tc->embed_lr_scale, 0.f, 1};
+  a.seg[1] = {c->n_embed, c->n_matrix_end, lr * tc->matrix_lr_scale, tc->weight_decay, 1};
+  a.seg[2] = {c->n_matrix_end, c->n_params, lr, 0.f, 0};
+  a.beta1 = tc->beta1;
+  a.beta2 = tc->beta2;
+  a.eps = tc->eps;
+  a.bc1 = 1.0f / (1.0f - powi_f32(tc->beta1, t));
+  a.bc2 = 1.0f / (1.0f - powi_f32(tc->beta2, t));
+  a.grad_scale = grad_scale;
+  a.norm = d_norm;
+  a.gsc = gsc;
+  a.clip = clip;
+  RT_OTHER(1, rt::adam_step(a, c->stream), "adam");
+  return RT_OK;
+}
+
+int check_train(rt_ctx* c) {
+  if (!c) return RT_ERR_ARG;
+  if (forward_only(c)) return set_err(c, RT_ERR_STATE, "context was created forward-only");
+  return RT_OK;
+}
+
+}  // namespace
+
+// ================================================================ C ABI
+static thread_local std::string g_create_error;
+
+extern "C" {
+
+// rt_last_error(NULL) reports why the last rt_ctx_create on this thread failed.
+RT_API const char* rt_last_error(const rt_ctx* c) { return c ? c->last_error.c_str() : g_create_error.c_str(); }
+
+RT_API int rt_lcg_fill(float* out, int64_t n, float scale) {
+  if (!out || n < 0) return RT_ERR_ARG;
+  uint64_t seed = 42ull + static_cast<uint64_t>(n);  // crates/engine/src/layer.rs:404-413
+  for (int64_t i = 0; i < n; ++i) {
+    seed = seed * 6364136223846793005ull + 1442695040888963407ull;
+    const float r =
+        (static_cast<float>(static_cast<uint32_t>(seed >> 32)) / static_cast<float>(UINT32_MAX)) * 2.0f - 1.0f;
+    out[i] = r * scale;
+  }
+  return RT_OK;
+}
+
+RT_API float rt_learning_rate(uint32_t step, const rt_train_config* tc) {
+  if (!tc) return 0.f;
+  if (step < tc->warmup_steps) return tc->max_lr * static_cast<float>(step + 1) / static_cast<float>(tc->warmup_steps);
+  const float decay = static_cast<float>(step - tc->warmup_steps) / static_cast<float>(tc->total_steps - tc->warmup_steps);
+  const float min_lr = tc->max_lr * tc->min_lr_frac;
+  return min_lr + 0.5f * (1.0f + cosf(3.14159265358979323846f * decay)) * (tc->max_lr - min_lr);
+}
+
+RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch, int flags, rt_ctx** out) {
+  if (!cfgp || !out || max_batch <= 0) return RT_ERR_ARG;
+  *out = nullptr;
+  const rt_model_config cfg = *cfgp;
+  rt_ctx* c = new rt_ctx();
+  c->cfg = cfg;
+  c->device = device;
+  c->max_batch = max_batch;
+  c->flags = flags;
+  auto bail = [&](int code, const std::string& msg) {
+    g_create_error = msg;
+    rt_ctx_destroy(c);
+    return code;
+  };
+  if (cfg.hd != 128 || cfg.heads * cfg.hd != cfg.dim || cfg.q_dim != cfg.dim || cfg.kv_dim != cfg.dim ||
+      cfg.kv_heads != cfg.heads || cfg.seq % 128 != 0 || cfg.dim % 128 != 0 || cfg.hidden % 64 != 0 ||
+      cfg.vocab % 64 != 0 || cfg.nlayers <= 0 || cfg.dim > 8192 || cfg.vocab > 8192)
+    return bail(RT_ERR_SHAPE, "unsupported model shape");
+  if (cudaSetDevice(device) != cudaSuccess) return bail(RT_ERR_CUDA, "cudaSetDevice");
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return bail(RT_ERR_CUDA, "stream");
+  for (auto& e : c->ev) cudaEventCreate(&e);
+
+  const int64_t D = cfg.dim, H = cfg.hidden, V = cfg.vocab, S = cfg.seq, L = cfg.nlayers, Q = cfg.q_dim;
+  const int64_t M = int64_t(max_batch) * S;
+  // parameter layout
+  c->n_embed = V * D;
+  int64_t off = c->n_embed;
+  c->layer_off.resize(L);
+  for (int64_t l = 0; l < L; ++l) {
+    auto& o = c->layer_off[l];
+    o.wqkv = off;
+    off += D * 3 * D;
+    o.wo = off;
+    off += Q * D;
+    o.w13 = off;
+    off += D * 2 * H;
+    o.w2 = off;
+    off += D * H;
+  }
+  c->n_matrix_end = off;
+  c->off_gamma_final = off;
+  off += D;
+  for (int64_t l = 0; l < L; ++l) {
+    c->layer_off[l].gamma1 = off;
+    off += D;
+    c->layer_off[l].gamma2 = off;
+    off += D;
+  }
+  c->n_params = off;
+
+  const bool fo = (flags & RT_CTX_FORWARD_ONLY) != 0;
+  bool ok = true;
+  auto need = [&](void* p) {
+    if (!p) ok = false;
+  };
+  c->d_err = dalloc<int>(c, 1);
+  need(c->d_err);
+  if (fo) {
+    c->params = dalloc<float>(c, c->n_embed + (c->n_params - c->n_matrix_end));
+    need(c->params);
+  } else {
+    c->params = dalloc<float>(c, c->n_params);
+    c->grads = dalloc<float>(c, c->n_params);
+    c->mom1 = dalloc<float>(c, c->n_params);
+    c->mom2 = dalloc<float>(c, c->n_params);
+    need(c->params);
+    need(c->grads);
+    need(c->mom1);
+    need(c->mom2);
+  }
+  c->params_bf16 = dalloc<bf16>(c, c->n_matrix_end);
+  need(c->params_bf16);
+  const int nact = fo ? 1 : static_cast<int>(L);
+  c->acts.resize(nact);
+  for (auto& A : c->acts) {
+    A.x = dalloc<float>(c, M * D);
+    A.xn = dalloc<bf16>(c, M * D);
+    A.rms1 = dalloc<float>(c, M);
+    A.qkv = dalloc<bf16>(c, M * 3 * D);
+    A.attn = dalloc<bf16>(c, M * D);
+    A.lse2 = dalloc<float>(c, M * cfg.heads);
+    A.x2 = dalloc<float>(c, M * D);
+    A.x2n = dalloc<bf16>(c, M * D);
+    A.rms2 = dalloc<float>(c, M);
+    A.h13 = dalloc<bf16>(c, M * 2 * H);
+    A.gate = dalloc<bf16>(c, M * H);
+    for (void* p : {(void*)A.x, (void*)A.xn, (void*)A.rms1, (void*)A.qkv, (void*)A.attn, (void*)A.lse2, (void*)A.x2,
+                    (void*)A.x2n, (void*)A.rms2, (void*)A.h13, (void*)A.gate})
+      need(p);
+  }
+  c->x_out = dalloc<float>(c, M * D);
+  c->xf = dalloc<bf16>(c, M * D);
+  c->rms_f = dalloc<float>(c, M);
+  c->logits = dalloc<float>(c, M * V);
+  c->row_loss = dalloc<float>(c, M);
+  c->row_lse = dalloc<float>(c, M);
+  c->d_loss = dalloc<float>(c, 4);
+  c->d_norm = dalloc<float>(c, 4);
+  c->norm_partials = dalloc<float>(c, rt::sumsq_partials_count());
+  c->dy_a = dalloc<float>(c, M * D);
+  for (void* p : {(void*)c->x_out, (void*)c->xf, (void*)c->rms_f, (void*)c->logits, (void*)c->row_loss,
+                  (void*)c->row_lse, (void*)c->d_loss, (void*)c->d_norm, (void*)c->norm_partials, (void*)c->dy_a})
+    need(p);
+  if (!fo) {
+    c->dl = dalloc<bf16>(c, M * V);
+    c->dy_b = dalloc<float>(c, M * D);
+    c->dx_tmp = dalloc<float>(c, M * D);
+    c->dx2 = dalloc<float>(c, M * D);
+    c->dffn = dalloc<bf16>(c, M * D);
+    c->dx2s = dalloc<bf16>(c, M * D);
+    c->da = dalloc<bf16>(c, M * D);
+    c->dh13 = dalloc<bf16>(c, M * 2 * H);
+    c->dqkv = dalloc<bf16>(c, M * 3 * D);
+    c->dvec = dalloc<float>(c, M * cfg.heads);
+    c->dgamma_part = dalloc<float>(c, int64_t(rt::rmsnorm_bwd_blocks(static_cast<int>(M))) * D);
+    for (void* p : {(void*)c->dl, (void*)c->dy_b, (void*)c->dx_tmp, (void*)c->dx2, (void*)c->dffn, (void*)c->dx2s,
+                    (void*)c->da, (void*)c->dh13, (void*)c->dqkv, (void*)c->dvec, (void*)c->dgamma_part})
+      need(p);
+  }
+  c->d_tokens = dalloc<uint32_t>(c, M);
+  c->d_targets = dalloc<uint32_t>(c, M);
+  c->d_perm = dalloc<int32_t>(c, M);
+  c->d_seg_start = dalloc<int32_t>(c, M + 1);
+  c->d_seg_tok = dalloc<uint32_t>(c, M);
+  c->rope_cos_f = dalloc<float>(c, S * 64);
+  c->rope_sin_f = dalloc<float>(c, S * 64);
+  c->rope_cos_b = dalloc<float>(c, S * 64);
+  c->rope_sin_b = dalloc<float>(c, S * 64);
+  for (void* p : {(void*)c->d_tokens, (void*)c->d_targets, (void*)c->d_perm, (void*)c->d_seg_start,
+                  (void*)c->d_seg_tok, (void*)c->rope_cos_f, (void*)c->rope_sin_f, (void*)c->rope_cos_b,
+                  (void*)c->rope_sin_b})
+    need(p);
+  if (!ok) return bail(RT_ERR_OOM, "device allocation failed");
+  c->h_stage_bytes = sizeof(uint32_t) * (5 * M + 2);
+  if (cudaMallocHost(&c->h_stage, c->h_stage_bytes) != cudaSuccess) return bail(RT_ERR_OOM, "pinned staging");
+  if (cudaMallocHost(reinterpret_cast<void**>(&c->h_loss), 4 * sizeof(float)) != cudaSuccess)
+    return bail(RT_ERR_OOM, "pinned loss");
+  cudaMemset(c->d_err, 0, sizeof(int));
+  std::vector<float> cf, sf, cb, sb;
+  compute_rope_tables(cfg, cf, sf, cb, sb);
+  cudaMemcpy(c->rope_cos_f, cf.data(), sizeof(float) * cf.size(), cudaMemcpyHostToDevice);
+  cudaMemcpy(c->rope_sin_f, sf.data(), sizeof(float) * sf.size(), cudaMemcpyHostToDevice);
+  cudaMemcpy(c->rope_cos_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice);
+  cudaMemcpy(c->rope_sin_b, sb.data(), sizeof(float) * sb.size(), cudaMemcpyHostToDevice);
+  if (cudaDeviceSynchronize() != cudaSuccess) return bail(RT_ERR_CUDA, "init");
+  *out = c;
+  return RT_OK;
+}
+
+RT_API int rt_ctx_destroy(rt_ctx* c) {
+  if (!c) return RT_ERR_ARG;
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->nccl) {
+    if (c->nccl->comm) {
+      if (rt::NcclApi* api = rt::nccl_api()) api->commDestroy(c->nccl->comm);
+    }
+    delete c->nccl;
+  }
+  for (void* p : c->allocations) cudaFree(p);
+  if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->h_loss) cudaFreeHost(c->h_loss);
+  for (auto& e : c->ev)
+    if (e) cudaEventDestroy(e);
+  for (auto e : c->event_pool) cudaEventDestroy(e);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+  return RT_OK;
+}
+
+RT_API int rt_ctx_device_bytes(const rt_ctx* c, int64_t* out) {
+  if (!c || !out) return RT_ERR_ARG;
+  *out = c->device_bytes;
+  return RT_OK;
+}
+
+RT_API int rt_weights_upload(rt_ctx* c, const rt_model_ptrs* w) {
+  if (!c || !w) return RT_ERR_ARG;
+  cudaSetDevice(c->device);
+  const auto& cfg = c->cfg;
+  const int64_t D = cfg.dim;
+  int rc;
+  if (!forward_only(c)) {
+    if ((rc = arena_h2d(c, c->params, w))) return rc;
+    RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_matrix_end, c->stream), "cast bf16");
+  } else {
+    // compact fp32 [embed | gammas]; matrices go through a bounded fp32 staging buffer
+    RT_CUDA(cudaMemcpy(c->params, w->embed, sizeof(float) * c->n_embed, cudaMemcpyHostToDevice), "upload embed");
+    RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_embed, c->stream), "cast bf16");
+    float* gb = gamma_base(c);
+    RT_CUDA(cudaMemcpy(gb, w->gamma_final, sizeof(float) * D, cudaMemcpyHostToDevice), "gamma_final");
+    const int64_t biggest = std::max<int64_t>(D * 3 * D, D * 2 * cfg.hidden);
+    float* stage = nullptr;
+    RT_CUDA(cudaMalloc(&stage, sizeof(float) * biggest), "staging");
+    rc = 0;
+    for (int l = 0; l < cfg.nlayers && rc == 0; ++l) {
+      const auto& o = c->layer_off[l];
+      const rt_layer_ptrs& L = w->layers[l];
+      const int64_t H = cfg.hidden;
+      rc = 0;
+      if (!rc) rc = copy_block_h2d(c, stage, 3 * D, 0, L.wq, D, D);
+      if (!rc) rc = copy_block_h2d(c, stage, 3 * D, D, L.wk, D, D);
+      if (!rc) rc = copy_block_h2d(c, stage, 3 * D, 2 * D, L.wv, D, D);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.wqkv, D * 3 * D, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaMemcpy(stage, L.wo, sizeof(float) * D * D, cudaMemcpyHostToDevice) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.wo, D * D, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = copy_block_h2d(c, stage, 2 * H, 0, L.w1, D, H);
+      if (!rc) rc = copy_block_h2d(c, stage, 2 * H, H, L.w3, D, H);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.w13, D * 2 * H, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaMemcpy(stage, L.w2, sizeof(float) * D * H, cudaMemcpyHostToDevice) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.w2, D * H, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaMemcpy(gb + (o.gamma1 - c->n_matrix_end), L.gamma1, sizeof(float) * D, cudaMemcpyHostToDevice)
+                        ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaMemcpy(gb + (o.gamma2 - c->n_matrix_end), L.gamma2, sizeof(float) * D, cudaMemcpyHostToDevice)
+                        ? RT_ERR_CUDA : 0;
+      cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(stage);
+    if (rc) return set_err(c, rc, "forward-only upload failed");
+  }
+  RT_CUDA(cudaStreamSynchronize(c->stream), "upload sync");
+  return RT_OK;
+}
+
+RT_API int rt_weights_download(rt_ctx* c, const rt_model_ptrs* w) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  cudaSetDevice(c->device);
+  RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
+  return arena_d2h(c, c->params, w);
+}
+
+RT_API int rt_grads_download(rt_ctx* c, const rt_model_ptrs* g) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  cudaSetDevice(c->device);
+  if ((rc = materialize_zero_grads(c))) return rc;
+  RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
+  return arena_d2h(c, c->grads, g);
+}
+
+RT_API int rt_grads_upload(rt_ctx* c, const rt_model_ptrs* g) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  cudaSetDevice(c->device);
+  RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
+  if ((rc = arena_h2d(c, c->grads, g))) return rc;
+  c->grads_zero_pending = false;
+  return RT_OK;
+}
+
+RT_API int rt_opt_download(rt_ctx* c, const rt_model_ptrs* m, const rt_model_ptrs* v) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  cudaSetDevice(c->device);
+  RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
+  if ((rc = arena_d2h(c, c->mom1, m))) return rc;
+  return arena_d2h(c, c->mom2, v);
+}
+
+RT_API int rt_opt_upload(rt_ctx* c, const rt_model_ptrs* m, const rt_model_ptrs* v) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  cudaSetDevice(c->device);
+  RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
+  if ((rc = arena_h2d(c, c->mom1, m))) return rc;
+  return arena_h2d(c, c->mom2, v);
+}
+
+RT_API int rt_weights_init_normal(rt_ctx* c, uint64_t seed, float std) {
+  if (!c) return RT_ERR_ARG;
+  cudaSetDevice(c->device);
+  const int64_t D = c->cfg.dim;
+  const int64_t n_gam = c->n_params - c->n_matrix_end;
+  if (!forward_only(c)) {
+    RT_LAUNCH(rt::init_normal(c->params, c->n_matrix_end, seed, std, c->stream), "init normal");
+    RT_LAUNCH(rt::fill_f32(c->params + c->n_matrix_end, n_gam, 1.0f, c->stream), "init gammas");
+    RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_matrix_end, c->stream), "cast bf16");
+    RT_CUDA(cudaMemsetAsync(c->mom1, 0, sizeof(float) * c->n_params, c->stream), "zero m");
+    RT_CUDA(cudaMemsetAsync(c->mom2, 0, sizeof(float) * c->n_params, c->stream), "zero v");
+    c->grads_zero_pending = true;
+  } else {
+    // embed straight into the compact fp32 buffer, matrices through a bounded staging buffer
+    RT_LAUNCH(rt::init_normal(c->params, c->n_embed, seed, std, c->stream), "init embed");
+    RT_LAUNCH(rt::fill_f32(gamma_base(c), n_gam, 1.0f, c->stream), "init gammas");
+    RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_embed, c->stream), "cast embed");
+    const int64_t chunk = int64_t(64) << 20;  // elements
+    float* stage = nullptr;
+    RT_CUDA(cudaMalloc(&stage, sizeof(float) * chunk), "staging");
+    for (int64_t b = c->n_embed; b < c->n_matrix_end; b += chunk) {
+      const int64_t n = std::min(chunk, c->n_matrix_end - b);
+      // the same counter stream as a training context: element i of the arena
+      int rc1 = rt::init_normal(stage, n, seed ^ (0x9E3779B97F4A7C15ull * uint64_t(b / chunk + 1)), std, c->stream);
+      int rc2 = rt::cast_bf16(stage, c->params_bf16 + b, n, c->stream);
+      if (rc1 || rc2) {
+        cudaFree(stage);
+        return set_err(c, RT_ERR_CUDA, "init normal (forward-only)");
+      }
+    }
+    cudaStreamSynchronize(c->stream);
+    cudaFree(stage);
+  }
+  (void)D;
+  RT_CUDA(cudaStreamSynchronize(c->stream), "init sync");
+  return RT_OK;
+}
+
+RT_API int rt_forward(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets, int batch, float softcap,
+                      float* loss_out, float* per_token_loss) {
+  if (!c || !tokens || !targets) return RT_ERR_ARG;
+  if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
+  cudaSetDevice(c->device);
+  int rc;
+  if ((rc = upload_tokens(c, tokens, targets, batch))) return rc;
+  if ((rc = forward_impl(c, batch, softcap))) return rc;
+  RT_CUDA(cudaMemcpyAsync(c->h_loss, c->d_loss, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss d2h");
+  if ((rc = wait_stream(c))) return rc;
+  if (loss_out) *loss_out = c->h_loss[0];
+  if (per_token_loss)
+    RT_CUDA(cudaMemcpy(per_token_loss, c->row_loss, sizeof(float) * batch * c->cfg.seq, cudaMemcpyDeviceToHost),
+            "per-token loss");
+  if (!std::isfinite(c->h_loss[0])) return set_err(c, RT_ERR_NONFINITE, "loss is not finite");
+  return RT_OK;
+}
+
+RT_API int rt_logits_download(rt_ctx* c, float* logits) {
+  if (!c || !logits) return RT_ERR_ARG;
+  if (!c->fwd_done) return set_err(c, RT_ERR_STATE, "no forward pass yet");
+  cudaSetDevice(c->device);
+  const int64_t M = int64_t(c->cur_batch) * c->cfg.seq, V = c->cfg.vocab;
+  RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
+  if (c->last_softcap > 0.f) {  // report the capped logits, as the reference stores them
+    std::vector<float> h(M * V);
+    RT_CUDA(cudaMemcpy(h.data(), c->logits, sizeof(float) * M * V, cudaMemcpyDeviceToHost), "logits");
+    const float sc = c->last_softcap;
+    for (int64_t i = 0; i < M * V; ++i) logits[i] = sc * tanhf(h[i] * (1.0f / sc));
+    return RT_OK;
+  }
+  RT_CUDA(cudaMemcpy(logits, c->logits, sizeof(float) * M * V, cudaMemcpyDeviceToHost), "logits");
+  return RT_OK;
+}
+
+RT_API int rt_backward(rt_ctx* c, float softcap, float loss_scale) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (!c->fwd_done) return set_err(c, RT_ERR_STATE, "backward before forward");
+  cudaSetDevice(c->device);
+  if ((rc = backward_impl(c, softcap, loss_scale))) return rc;
+  return wait_stream(c);
+}
+
+RT_API int rt_grads_zero(rt_ctx* c) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  c->grads_zero_pending = true;
+  return RT_OK;
+}
+
+RT_API int rt_grad_norm(rt_ctx* c, float* norm_out) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  cudaSetDevice(c->device);
+  if ((rc = materialize_zero_grads(c))) return rc;
+  RT_OTHER(2, rt::sumsq_norm(c->grads, c->n_params, c->norm_partials, c->d_norm, c->stream), "grad norm");
+  RT_CUDA(cudaMemcpyAsync(c->h_loss + 1, c->d_norm, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "norm d2h");
+  if ((rc = wait_stream(c))) return rc;
+  if (norm_out) *norm_out = c->h_loss[1];
+  return RT_OK;
+}
+
+RT_API int rt_clip_grads(rt_ctx* c, float max_norm) {
+  float norm = 0.f;
+  int rc;
+  if ((rc = rt_grad_norm(c, &norm))) return rc;
+  if (norm > max_norm) {
+    RT_OTHER(1, rt::scale_f32(c->grads, c->grads, c->n_params, max_norm / norm, c->stream), "clip");
+    return wait_stream(c);
+  }
+  return RT_OK;
+}
+
+RT_API int rt_update_weights(rt_ctx* c, uint32_t t, float lr, const rt_train_config* tc, float grad_scale) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (!tc || t == 0) return set_err(c, RT_ERR_ARG, "train config missing or t == 0");
+  cudaSetDevice(c->device);
+  if ((rc = materialize_zero_grads(c))) return rc;
+  cudaEventRecord(c->ev[6], c->stream);
+  if ((rc = adam_impl(c, t, lr, tc, grad_scale, nullptr, 0.f, 0.f))) return rc;
+  cudaEventRecord(c->ev[7], c->stream);
+  return wait_stream(c);
+}
+
+RT_API int rt_train_step(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets, int batch, uint32_t step,
+                         const rt_train_config* tc, float* loss_out) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (!tokens || !targets || !tc) return set_err(c, RT_ERR_ARG, "null argument");
+  if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
+  cudaSetDevice(c->device);
+  if ((rc = upload_tokens(c, tokens, targets, batch))) return rc;
+  c->grads_zero_pending = true;  // grads.zero_out() (full_model.rs:675)
+  if ((rc = forward_impl(c, batch, tc->softcap))) return rc;
+  if ((rc = backward_impl(c, tc->softcap, tc->loss_scale))) return rc;
+  cudaEventRecord(c->ev[4], c->stream);
+  if (c->world > 1 && c->dist_mode == RT_DIST_DATA_PARALLEL) {
+    if ((rc = rt_grad_allreduce(c))) return rc;
+  }
+  cudaEventRecord(c->ev[5], c->stream);
+  cudaEventRecord(c->ev[6], c->stream);
+  RT_OTHER(2, rt::sumsq_norm(c->grads, c->n_params, c->norm_partials, c->d_norm, c->stream), "grad norm");
+  const float gsc = 1.0f / (static_cast<float>(batch) * static_cast<float>(c->world) * tc->loss_scale);
+  const float lr = rt_learning_rate(step, tc);
+  if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip))) return rc;
+  cudaEventRecord(c->ev[7], c->stream);
+  RT_CUDA(cudaMemcpyAsync(c->h_loss, c->d_loss, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss d2h");
+  if ((rc = wait_stream(c))) return rc;
+  if (loss_out) *loss_out = c->h_loss[0];
+  if (!std::isfinite(c->h_loss[0])) return set_err(c, RT_ERR_NONFINITE, "loss is not finite");
+  return RT_OK;
+}
+
+RT_API int rt_nccl_unique_id(uint8_t* out128) {
+  if (!out128) return RT_ERR_ARG;
+  rt::NcclApi* api = rt::nccl_api();
+  if (!api) return RT_ERR_NCCL;
+  ncclUniqueId id;
+  if (api->getUniqueId(&id) != ncclSuccess) return RT_ERR_NCCL;
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+  memcpy(out128, &id, 128);
+  return RT_OK;
+}
+
+RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms) {
+  if (!c || world <= 0 || rank < 0 || rank >= world) return RT_ERR_ARG;
+  if (mode != RT_DIST_DATA_PARALLEL && mode != RT_DIST_TENSOR_PARALLEL) return RT_ERR_ARG;
+  if (mode == RT_DIST_TENSOR_PARALLEL)
+    return set_err(c, RT_ERR_STATE, "tensor-parallel contexts are not supported by this build");
+  c->world = world;
+  c->rank = rank;
+  c->dist_mode = mode;
+  c->timeout_ms = timeout_ms;
+  if (world == 1) return RT_OK;
+  if (!unique_id128) return RT_ERR_ARG;
+  rt::NcclApi* api = rt::nccl_api();
+  if (!api) return set_err(c, RT_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  cudaSetDevice(c->device);
+  ncclUniqueId id;
+  memcpy(&id, unique_id128, 128);
+  c->nccl = new rt::NcclState();
+  ncclResult_t r = api->commInitRank(&c->nccl->comm, world, id, rank);
+  if (r != ncclSuccess) {
+    c->nccl->comm = nullptr;
+    return set_err(c, RT_ERR_NCCL, std::string("ncclCommInitRank: ") + api->errorString(r));
+  }
+  return RT_OK;
+}
+
+RT_API int rt_grad_allreduce(rt_ctx* c) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (c->world == 1) return RT_OK;
+  if (!c->nccl || !c->nccl->comm) return set_err(c, RT_ERR_NCCL, "no communicator (aborted or not initialised)");
+  if ((rc = materialize_zero_grads(c))) return rc;
+  rt::NcclApi* api = rt::nccl_api();
+  ncclResult_t r = api->allReduce(c->grads, c->grads, static_cast<size_t>(c->n_params), ncclFloat32, ncclSum,
+                                  c->nccl->comm, c->stream);
+  if (r != ncclSuccess) return set_err(c, RT_ERR_NCCL, std::string("ncclAllReduce: ") + api->errorString(r));
+  return RT_OK;
+}
+
+RT_API int rt_profile(rt_ctx* c, int enable) {
+  if (!c) return RT_ERR_ARG;
+  cudaStreamSynchronize(c->stream);
+  c->kevents.clear();
+  c->event_pool_used = 0;
+  const int64_t launches = c->acc.kernel_launches;
+  c->acc = rt_timings{};
+  c->acc.kernel_launches = launches;
+  c->profiling = enable != 0;
+  return RT_OK;
+}
+
+RT_API int rt_get_timings(rt_ctx* c, rt_timings* out) {
+  if (!c || !out) return RT_ERR_ARG;
+  cudaStreamSynchronize(c->stream);
+  if (c->profiling) harvest_kernel_events(c);
+  float ms = 0.f;
+  rt_timings t = c->acc;
+  if (cudaEventElapsedTime(&ms, c->ev[0], c->ev[1]) == cudaSuccess) t.fwd_ms = ms;
+  if (cudaEventElapsedTime(&ms, c->ev[2], c->ev[3]) == cudaSuccess) t.bwd_ms = ms;
+  if (cudaEventElapsedTime(&ms, c->ev[4], c->ev[5]) == cudaSuccess) t.comm_ms = ms;
+  if (cudaEventElapsedTime(&ms, c->ev[6], c->ev[7]) == cudaSuccess) t.opt_ms = ms;
+  *out = t;
+  return RT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,130 @@
+// Internal runtime state of an rt_ctx (librustane_cuda).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "rustane_cuda.h"
+
+namespace rt {
+
+using bf16 = __nv_bfloat16;
+
+// Offsets (elements) of one layer's tensors inside the parameter arena.
+// Wqkv is [dim, 3*dim] with rows wq[i,:] | wk[i,:] | wv[i,:]; W13 is
+// [dim, 2*hidden] with rows w1[i,:] | w3[i,:]; Wo [q_dim, dim]; W2 [dim, hidden].
+struct LayerOffsets {
+  int64_t wqkv, wo, w13, w2, gamma1, gamma2;
+};
+
+// Activations of one layer kept for the backward pass (token-major, M rows).
+struct LayerActs {
+  float* x = nullptr;      // [M, D] layer input (fp32 residual stream)
+  bf16* xn = nullptr;      // [M, D] RMSNorm1 output
+  float* rms1 = nullptr;   // [M]
+  bf16* qkv = nullptr;     // [M, 3D] roped Q, K and V
+  bf16* attn = nullptr;    // [M, D] attention output
+  float* lse2 = nullptr;   // [B, heads, S]
+  float* x2 = nullptr;     // [M, D] x + alpha * attn Wo
+  bf16* x2n = nullptr;     // [M, D] RMSNorm2 output
+  float* rms2 = nullptr;   // [M]
+  bf16* h13 = nullptr;     // [M, 2H] h1 | h3
+  bf16* gate = nullptr;    // [M, H] silu(h1) * h3
+};
+
+struct KernelEvent {
+  int kind;  // 0 gemm, 1 attention, 2 other
+  double flops;
+  cudaEvent_t a, b;
+};
+
+struct NcclState;
+
+}  // namespace rt
+
+struct rt_ctx {
+  rt_model_config cfg{};
+  int device = 0;
+  int max_batch = 0;
+  int flags = 0;
+  cudaStream_t stream = nullptr;
+  std::string last_error;
+  int* d_err = nullptr;
+
+  // parameter arenas (elements): [embed | matrices | gammas]
+  int64_t n_params = 0, n_embed = 0, n_matrix_end = 0;
+  int64_t off_gamma_final = 0;
+  std::vector<rt::LayerOffsets> layer_off;
+  float* params = nullptr;  // fp32 master (forward-only: gammas + embed only are meaningful)
+  float* grads = nullptr;
+  float* mom1 = nullptr;
+  float* mom2 = nullptr;
+  rt::bf16* params_bf16 = nullptr;  // [embed | matrices]
+
+  // activations
+  std::vector<rt::LayerActs> acts;
+  float* x_out = nullptr;  // [M, D] final layer output (pre final norm)
+  rt::bf16* xf = nullptr;  // [M, D] final-norm output
+  float* rms_f = nullptr;  // [M]
+  float* logits = nullptr;  // [M, V]
+  float* row_loss = nullptr;
+  float* row_lse = nullptr;
+  float* d_loss = nullptr;  // [1]
+  float* d_norm = nullptr;  // [1]
+  float* norm_partials = nullptr;
+
+  // backward scratch
+  rt::bf16* dl = nullptr;    // [M, V]
+  float* dy_a = nullptr;     // [M, D]
+  float* dy_b = nullptr;     // [M, D]
+  float* dx_tmp = nullptr;   // [M, D]
+  float* dx2 = nullptr;      // [M, D]
+  rt::bf16* dffn = nullptr;  // [M, D] alpha * dy
+  rt::bf16* dx2s = nullptr;  // [M, D] alpha * dx2
+  rt::bf16* da = nullptr;    // [M, D]
+  rt::bf16* dh13 = nullptr;  // [M, 2H]
+  rt::bf16* dqkv = nullptr;  // [M, 3D]
+  float* dvec = nullptr;     // [B, heads, S]
+  float* dgamma_part = nullptr;
+
+  // tokens and the embedding-scatter segments
+  uint32_t* d_tokens = nullptr;
+  uint32_t* d_targets = nullptr;
+  int32_t* d_perm = nullptr;
+  int32_t* d_seg_start = nullptr;
+  uint32_t* d_seg_tok = nullptr;
+  int nseg = 0;
+  void* h_stage = nullptr;  // pinned staging for token uploads
+  size_t h_stage_bytes = 0;
+  float* h_loss = nullptr;  // pinned
+
+  // rope tables
+  float* rope_cos_f = nullptr;  // [S][hd/2]
+  float* rope_sin_f = nullptr;
+  float* rope_cos_b = nullptr;  // [hd/2][S]
+  float* rope_sin_b = nullptr;
+
+  // state
+  int cur_batch = 0;
+  bool fwd_done = false;
+  bool grads_zero_pending = true;
+  float last_softcap = 0.f;
+  int64_t device_bytes = 0;
+  std::vector<void*> allocations;
+
+  // distributed
+  int world = 1, rank = 0, dist_mode = -1, timeout_ms = 0;
+  rt::NcclState* nccl = nullptr;
+
+  // timing
+  cudaEvent_t ev[8] = {};
+  bool profiling = false;
+  std::vector<rt::KernelEvent> kevents;
+  std::vector<cudaEvent_t> event_pool;
+  size_t event_pool_used = 0;
+  rt_timings acc{};
+};
