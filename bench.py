@@ -1,0 +1,330 @@
+#!/usr/bin/env python
+"""Benchmark of rustane's language-model train step on B200.
+
+Workload: the 600M-class decoder (dim 1536, SwiGLU hidden
+4096, 20 layers, 12 heads x 128, seq 512, vocab 8192), per-GPU batch 8 of
+uniform-random token ids, weights N(0, 0.02) from seed 1234, fp32 master
+weights + AdamW state with bf16 compute.  One step = forward + cross-entropy +
+backward + [data-parallel gradient all-reduce] + grad-norm clip + AdamW.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) each rank drives one GPU; time is the max over ranks.
+Prints ONE JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "train-step tok/s & forward ms at 600M/5B/7B; TC util vs B200 bf16 peak"
+PUBLISHED_TOK_S = 533.0  # 600m-A train step, M4 Max ANE + CPU (results/2026-03-18_1830_param-sweep.md:37)
+SPEC_BF16_TFLOPS = 2250.0
+PER_GPU_BATCH = 8
+SEED_WEIGHTS = 1234
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def workload_cfg():
+    from rustane_b200 import ModelConfig
+    return ModelConfig.c600m()
+
+
+def workload_desc(cfg) -> str:
+    return (f"600M train step: dim {cfg.dim}, SwiGLU hidden {cfg.hidden}, {cfg.nlayers} layers, {cfg.heads} heads x "
+            f"{cfg.hd}, seq {cfg.seq}, vocab {cfg.vocab}, per-GPU batch {PER_GPU_BATCH}")
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = [ln.split(",") for ln in open(self.path).read().splitlines() if ln.strip()]
+        os.unlink(self.path)
+        sm, smax, power, reasons = [], None, [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            r = [x.strip() for x in r]
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+                power.append(float(r[3]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        under_load = [s for s, p in zip(sm, power) if p > 200.0] or sm
+        return {"sm_mhz": statistics.median(under_load) if under_load else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------ CPU oracle
+def oracle_step_seconds(cfg, n_steps: int, budget_s: float = 30.0):
+    """The CPU restatement of the reference train step (oracle/, fp32, host BLAS)
+    on one 512-token sequence per step.  Returns (seconds per step, threads, blas)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle as po
+    from rustane_b200.tensors import ModelOptState, ModelTensors
+    w = po.reference_init(cfg)
+    g, opt = ModelTensors.zeros(cfg), ModelOptState.zeros(cfg)
+    o = po.Oracle(cfg, 1)
+    rng = np.random.default_rng(1000)
+    tc = po.default_train_config()
+    times = []
+    t_all = time.perf_counter()
+    for i in range(n_steps):
+        tok = rng.integers(0, cfg.vocab, cfg.seq).astype(np.uint32)
+        tgt = rng.integers(0, cfg.vocab, cfg.seq).astype(np.uint32)
+        t0 = time.perf_counter()
+        o.train_step(w, g, opt, tok, tgt, i, tc)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    return times, po.lib().or_threads(), Path(po.lib().or_blas_name().decode()).name
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = workload_cfg()
+    W, K = args.warmup, args.steps
+    # warmup steps (untimed) then K timed steps, each one 512-token sequence
+    wt, threads, blas = oracle_step_seconds(cfg, W, budget_s=120.0)
+    tt, _, _ = oracle_step_seconds(cfg, K, budget_s=240.0)
+    per = statistics.mean(tt)
+    value = cfg.seq / per
+    sample = f"1 sequence x {cfg.seq} tokens of the 600M train step per step ({len(tt)} timed steps)"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": len(tt), "warmup": len(wt), "ms_per_step": per * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_desc(cfg) + " (CPU sample: batch 1)", "per_gpu_batch": 1,
+                   "seq_len": cfg.seq, "parallelism": "none (host CPU)"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample,
+                         "blas": blas},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference (Rust + Apple ANE/Accelerate) cannot run on Linux; its CPU path is timed "
+                 "through the fp32 C++ restatement in oracle/ with host OpenBLAS sgemm"),
+    }), flush=True)
+
+
+# ------------------------------------------------------------- our arm
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    W = max(args.warmup, 3)
+    K = args.steps
+
+    import torch
+    from rustane_b200 import CompiledKernels, TrainConfig, _lib
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    cfg = workload_cfg()
+    B, S = PER_GPU_BATCH, cfg.seq
+    k = CompiledKernels.compile(cfg, max_batch=B, device=local)
+    k.init_normal(seed=SEED_WEIGHTS, std=0.02)
+    if world > 1:
+        uid = [CompiledKernels.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        k.dist_init(world, rank, uid[0], _lib.RT_DIST_DATA_PARALLEL, timeout_ms=120000)
+
+    rng = np.random.default_rng(1000 + rank)
+    nslots = 4
+    batches = []
+    for slot in range(nslots):
+        tok = rng.integers(0, cfg.vocab, B * S).astype(np.uint32)
+        tgt = rng.integers(0, cfg.vocab, B * S).astype(np.uint32)
+        batches.append((tok, tgt))
+        k._check(_lib.lib().rt_stage_batch(k.handle, slot, tok.ctypes.data_as(_lib.c_uint32_p),
+                                           tgt.ctypes.data_as(_lib.c_uint32_p), B))
+    tc = TrainConfig()
+    c_tc = tc.to_c()
+    L = _lib.lib()
+    step = 0
+
+    def staged_steps(n):
+        nonlocal step
+        for _ in range(n):
+            k._check(L.rt_train_step_staged(k.handle, step % nslots, step, ctypes.byref(c_tc), None))
+            step += 1
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # -------- warm-up
+    staged_steps(W)
+    loss_w = ctypes.c_float()
+    k._check(L.rt_sync(k.handle, ctypes.byref(loss_w)))
+
+    # -------- timed region: device-resident inputs, CUDA events on the context stream
+    sp = ctypes.c_void_p()
+    k._check(L.rt_ctx_stream(k.handle, ctypes.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value)
+    k.profile(True)
+    launches0 = k.timings()["kernel_launches"]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        staged_steps(K)
+        ev1.record(stream)
+        loss_last = ctypes.c_float()
+        k._check(L.rt_sync(k.handle, ctypes.byref(loss_last)))
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ms_local)
+    tm = k.timings()
+    launches = tm["kernel_launches"] - launches0
+    k.profile(False)
+    ms_per_step = ms / K
+    tokens = world * B * S * K
+    value = tokens / (ms / 1e3)
+
+    # -------- end to end: host tokens through the public API every step
+    host_tok = [np.ascontiguousarray(b[0]) for b in batches]
+    host_tgt = [np.ascontiguousarray(b[1]) for b in batches]
+    h2d = ctypes.c_int64()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(K):
+        k.train_step(host_tok[i % nslots], host_tgt[i % nslots], step, tc)
+        step += 1
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    L.rt_last_h2d_bytes(k.handle, ctypes.byref(h2d))
+    e2e_value = tokens / e2e_s
+
+    # -------- roofline of the dominant kernel family (tcgen05 GEMM)
+    pk = peaks()
+    gemm_tflops = tm["gemm_flops"] / (tm["gemm_ms"] * 1e-3) / 1e12 if tm["gemm_ms"] > 0 else None
+    per_launch_flops = tm["gemm_flops"] / max(tm["gemm_launches"], 1)
+    model_flops = 3.0 * cfg.flops_per_token_fwd() * B * S  # per GPU per step (train = 3 x forward)
+    step_tflops = model_flops / (ms_per_step * 1e-3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "gemm_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+
+    result = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": workload_desc(cfg), "per_gpu_batch": B, "seq_len": S, "tokens_per_gpu_step": B * S,
+                   "parallelism": f"dp{world}", "weights": "N(0,0.02) seed 1234, fp32 master + AdamW state",
+                   "tokens": "uniform ids, seed 1000+rank",
+                   "l2": "not flushed: every step streams > 10 GB of weights/grads/optimizer state (>> 126 MB L2)"},
+        "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM (all projections, FFN, logits, data and weight grads)",
+                     "achieved": gemm_tflops, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                     "frac": (gemm_tflops / pk["bf16_sustained"]) if gemm_tflops else None,
+                     "traffic": traffic, "flops_per_launch": per_launch_flops,
+                     "launches": tm["gemm_launches"], "peak_source": pk["source"] + " sustained bf16"},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(h2d.value), "d2h_bytes_per_step": 4},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+        "step_breakdown_ms": {"fwd": tm["fwd_ms"], "bwd": tm["bwd_ms"], "allreduce": tm["comm_ms"],
+                              "norm_adam": tm["opt_ms"]},
+        "fwd_ms": tm["fwd_ms"],
+        "step_tflops": step_tflops,
+        "tc_util": {"vs_measured_peak": step_tflops / pk["bf16"], "vs_spec_2250": step_tflops / SPEC_BF16_TFLOPS},
+        "kernel_ms_per_step": {"gemm": tm["gemm_ms"] / K, "attention": tm["attn_ms"] / K, "other": tm["other_ms"] / K},
+        "loss_last": loss_last.value,
+        "vs_baseline_basis": "600m-A train step 533 tok/s, Apple M4 Max (BASELINE.md)",
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times, threads, blas = oracle_step_seconds(cfg, 2, budget_s=25.0)
+        per = statistics.mean(times)
+        result["cpu_baseline"] = {"value": cfg.seq / per, "unit": "tok/s", "cores": threads, "kind": "port",
+                                  "sample": f"{len(times)} train step(s) of 1 x {cfg.seq} tokens, 600M config",
+                                  "blas": blas}
+    k.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

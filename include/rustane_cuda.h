@@ -171,6 +171,21 @@ RT_API float rt_learning_rate(uint32_t step, const rt_train_config* tc);
 RT_API int rt_train_step(rt_ctx* ctx, const uint32_t* tokens, const uint32_t* targets, int batch, uint32_t step,
                          const rt_train_config* tc, float* loss_out);
 
+/* Device-resident inputs: upload a batch (tokens, targets and the embedding
+ * scatter segments) into slot `slot` ahead of time, then run steps on it with
+ * no host transfer.  rt_train_step_staged with loss_out == NULL returns
+ * without waiting (asynchronous); rt_sync waits, checks the device error word
+ * and optionally reads the last loss.  These are the train_step / forward_ws
+ * of full_model.rs with the input copy hoisted out of the step. */
+RT_API int rt_stage_batch(rt_ctx* ctx, int slot, const uint32_t* tokens, const uint32_t* targets, int batch);
+RT_API int rt_train_step_staged(rt_ctx* ctx, int slot, uint32_t step, const rt_train_config* tc, float* loss_out);
+RT_API int rt_forward_staged(rt_ctx* ctx, int slot, float softcap);
+RT_API int rt_sync(rt_ctx* ctx, float* loss_out);
+/* The context's CUDA stream (cudaStream_t) — every kernel of the context runs on it. */
+RT_API int rt_ctx_stream(const rt_ctx* ctx, void** stream_out);
+/* Bytes the last host-token call copied host -> device. */
+RT_API int rt_last_h2d_bytes(const rt_ctx* ctx, int64_t* out);
+
 /* ------------------------------------------------------- multi-GPU */
 
 /* NCCL unique id (128 bytes) for rank 0 to broadcast to the other ranks. */

@@ -73,6 +73,12 @@ SIGNATURES: dict[str, tuple] = {
     "rt_update_weights": (c_int, [c_void_p, c_uint32, c_float, P_TC, c_float]),
     "rt_learning_rate": (c_float, [c_uint32, P_TC]),
     "rt_train_step": (c_int, [c_void_p, c_uint32_p, c_uint32_p, c_int, c_uint32, P_TC, c_float_p]),
+    "rt_stage_batch": (c_int, [c_void_p, c_int, c_uint32_p, c_uint32_p, c_int]),
+    "rt_train_step_staged": (c_int, [c_void_p, c_int, c_uint32, P_TC, c_float_p]),
+    "rt_forward_staged": (c_int, [c_void_p, c_int, c_float]),
+    "rt_sync": (c_int, [c_void_p, c_float_p]),
+    "rt_ctx_stream": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "rt_last_h2d_bytes": (c_int, [c_void_p, ctypes.POINTER(c_int64)]),
     "rt_nccl_unique_id": (c_int, [c_uint8_p]),
     "rt_dist_init": (c_int, [c_void_p, c_int, c_int, c_uint8_p, c_int, c_int]),
     "rt_grad_allreduce": (c_int, [c_void_p]),

@@ -325,9 +325,18 @@ int materialize_zero_grads(rt_ctx* c) {
   return RT_OK;
 }
 
+void alloc_token_batch(rt_ctx* c, rt::TokenBatch& tb) {
+  const int64_t M = int64_t(c->max_batch) * c->cfg.seq;
+  tb.tokens = dalloc<uint32_t>(c, M);
+  tb.targets = dalloc<uint32_t>(c, M);
+  tb.perm = dalloc<int32_t>(c, M);
+  tb.seg_start = dalloc<int32_t>(c, M + 1);
+  tb.seg_tok = dalloc<uint32_t>(c, M);
+}
+
 // Tokens -> device, with the embedding-scatter segments built on the host
 // (counting sort by token, positions ascending within a token).
-int upload_tokens(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets, int batch) {
+int upload_tokens(rt_ctx* c, rt::TokenBatch& tb, const uint32_t* tokens, const uint32_t* targets, int batch) {
   const int M = batch * c->cfg.seq;
   const uint32_t V = static_cast<uint32_t>(c->cfg.vocab);
   for (int i = 0; i < M; ++i)
@@ -354,16 +363,19 @@ int upload_tokens(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets, in
   st_start[nseg] = M;
   std::vector<int32_t> fillpos(count.begin(), count.end() - 1);
   for (int i = 0; i < M; ++i) st_perm[fillpos[tokens[i]]++] = i;
-  c->nseg = nseg;
-  RT_CUDA(cudaMemcpyAsync(c->d_tokens, st_tok, sizeof(uint32_t) * M, cudaMemcpyHostToDevice, c->stream), "tokens");
+  tb.nseg = nseg;
+  tb.batch = batch;
+  RT_CUDA(cudaMemcpyAsync(tb.tokens, st_tok, sizeof(uint32_t) * M, cudaMemcpyHostToDevice, c->stream), "tokens");
   if (targets)
-    RT_CUDA(cudaMemcpyAsync(c->d_targets, st_tgt, sizeof(uint32_t) * M, cudaMemcpyHostToDevice, c->stream),
+    RT_CUDA(cudaMemcpyAsync(tb.targets, st_tgt, sizeof(uint32_t) * M, cudaMemcpyHostToDevice, c->stream),
             "targets");
-  RT_CUDA(cudaMemcpyAsync(c->d_perm, st_perm, sizeof(int32_t) * M, cudaMemcpyHostToDevice, c->stream), "perm");
-  RT_CUDA(cudaMemcpyAsync(c->d_seg_start, st_start, sizeof(int32_t) * (nseg + 1), cudaMemcpyHostToDevice, c->stream),
+  RT_CUDA(cudaMemcpyAsync(tb.perm, st_perm, sizeof(int32_t) * M, cudaMemcpyHostToDevice, c->stream), "perm");
+  RT_CUDA(cudaMemcpyAsync(tb.seg_start, st_start, sizeof(int32_t) * (nseg + 1), cudaMemcpyHostToDevice, c->stream),
           "seg_start");
-  RT_CUDA(cudaMemcpyAsync(c->d_seg_tok, st_segtok, sizeof(uint32_t) * nseg, cudaMemcpyHostToDevice, c->stream),
+  RT_CUDA(cudaMemcpyAsync(tb.seg_tok, st_segtok, sizeof(uint32_t) * nseg, cudaMemcpyHostToDevice, c->stream),
           "seg_tok");
+  c->h2d_bytes_last = int64_t(sizeof(uint32_t)) * (targets ? 2 * M : M) + int64_t(sizeof(int32_t)) * (M + nseg + 1) +
+                      int64_t(sizeof(uint32_t)) * nseg;
   return RT_OK;
 }
 
@@ -428,7 +440,7 @@ int forward_impl(rt_ctx* c, int batch, float softcap) {
   int rc;
   cudaEventRecord(c->ev[0], c->stream);
   float* x0 = c->acts[0].x;
-  RT_OTHER(1, rt::embed_gather(c->params, c->d_tokens, x0, M, D, V, c->d_err, c->stream), "embed gather");
+  RT_OTHER(1, rt::embed_gather(c->params, c->cur->tokens, x0, M, D, V, c->d_err, c->stream), "embed gather");
   float* x = x0;
   for (int l = 0; l < cfg.nlayers; ++l) {
     const rt::LayerActs& A = forward_only(c) ? c->acts[0] : c->acts[l];
@@ -450,7 +462,7 @@ int forward_impl(rt_ctx* c, int batch, float softcap) {
     g.epi = rt::kEpiF32; g.out = c->logits; g.ldo = V;
     if ((rc = gemm(c, g, "logits"))) return rc;
   }
-  RT_OTHER(1, rt::ce_forward(c->logits, c->d_targets, c->row_loss, c->row_lse, M, V, softcap, c->stream), "ce fwd");
+  RT_OTHER(1, rt::ce_forward(c->logits, c->cur->targets, c->row_loss, c->row_lse, M, V, softcap, c->stream), "ce fwd");
   RT_OTHER(1, rt::mean_reduce(c->row_loss, M, c->d_loss, c->stream), "loss mean");
   cudaEventRecord(c->ev[1], c->stream);
   c->cur_batch = batch;
@@ -473,7 +485,7 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   int rc;
   cudaEventRecord(c->ev[2], c->stream);
   // dlogits * loss_scale (full_model.rs:265-276); CE mean over seq per sequence (cross_entropy.rs:92-95)
-  RT_OTHER(1, rt::ce_backward(c->logits, c->row_lse, c->d_targets, c->dl, M, V, softcap, loss_scale / S, c->stream),
+  RT_OTHER(1, rt::ce_backward(c->logits, c->row_lse, c->cur->targets, c->dl, M, V, softcap, loss_scale / S, c->stream),
            "ce bwd");
   {  // dx_final = dl * E   (full_model.rs:279-289)
     rt::GemmArgs g;
@@ -587,7 +599,7 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
     std::swap(dy, dy_next);
   }
   // embedding scatter-add (full_model.rs:330)
-  RT_OTHER(1, rt::embed_scatter(dy, c->d_perm, c->d_seg_start, c->d_seg_tok, c->nseg, Gr, D, c->stream),
+  RT_OTHER(1, rt::embed_scatter(dy, c->cur->perm, c->cur->seg_start, c->cur->seg_tok, c->cur->nseg, Gr, D, c->stream),
            "embed scatter");
   cudaEventRecord(c->ev[3], c->stream);
   c->grads_zero_pending = false;
@@ -780,17 +792,13 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
                     (void*)c->da, (void*)c->dh13, (void*)c->dqkv, (void*)c->dvec, (void*)c->dgamma_part})
       need(p);
   }
-  c->d_tokens = dalloc<uint32_t>(c, M);
-  c->d_targets = dalloc<uint32_t>(c, M);
-  c->d_perm = dalloc<int32_t>(c, M);
-  c->d_seg_start = dalloc<int32_t>(c, M + 1);
-  c->d_seg_tok = dalloc<uint32_t>(c, M);
+  alloc_token_batch(c, c->io);
   c->rope_cos_f = dalloc<float>(c, S * 64);
   c->rope_sin_f = dalloc<float>(c, S * 64);
   c->rope_cos_b = dalloc<float>(c, S * 64);
   c->rope_sin_b = dalloc<float>(c, S * 64);
-  for (void* p : {(void*)c->d_tokens, (void*)c->d_targets, (void*)c->d_perm, (void*)c->d_seg_start,
-                  (void*)c->d_seg_tok, (void*)c->rope_cos_f, (void*)c->rope_sin_f, (void*)c->rope_cos_b,
+  for (void* p : {(void*)c->io.tokens, (void*)c->io.targets, (void*)c->io.perm, (void*)c->io.seg_start,
+                  (void*)c->io.seg_tok, (void*)c->rope_cos_f, (void*)c->rope_sin_f, (void*)c->rope_cos_b,
                   (void*)c->rope_sin_b})
     need(p);
   if (!ok) return bail(RT_ERR_OOM, "device allocation failed");
@@ -973,7 +981,8 @@ RT_API int rt_forward(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets
   if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
   cudaSetDevice(c->device);
   int rc;
-  if ((rc = upload_tokens(c, tokens, targets, batch))) return rc;
+  if ((rc = upload_tokens(c, c->io, tokens, targets, batch))) return rc;
+  c->cur = &c->io;
   if ((rc = forward_impl(c, batch, softcap))) return rc;
   RT_CUDA(cudaMemcpyAsync(c->h_loss, c->d_loss, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss d2h");
   if ((rc = wait_stream(c))) return rc;
@@ -1053,14 +1062,13 @@ RT_API int rt_update_weights(rt_ctx* c, uint32_t t, float lr, const rt_train_con
   return wait_stream(c);
 }
 
-RT_API int rt_train_step(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets, int batch, uint32_t step,
-                         const rt_train_config* tc, float* loss_out) {
+// Everything of train_step after the batch is on the device; async unless
+// loss_out is given (then the loss is copied back and the stream waited on).
+static int train_step_device(rt_ctx* c, const rt::TokenBatch& tb, uint32_t step, const rt_train_config* tc,
+                             float* loss_out) {
   int rc;
-  if ((rc = check_train(c))) return rc;
-  if (!tokens || !targets || !tc) return set_err(c, RT_ERR_ARG, "null argument");
-  if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
-  cudaSetDevice(c->device);
-  if ((rc = upload_tokens(c, tokens, targets, batch))) return rc;
+  const int batch = tb.batch;
+  c->cur = &tb;
   c->grads_zero_pending = true;  // grads.zero_out() (full_model.rs:675)
   if ((rc = forward_impl(c, batch, tc->softcap))) return rc;
   if ((rc = backward_impl(c, tc->softcap, tc->loss_scale))) return rc;
@@ -1075,10 +1083,82 @@ RT_API int rt_train_step(rt_ctx* c, const uint32_t* tokens, const uint32_t* targ
   const float lr = rt_learning_rate(step, tc);
   if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip))) return rc;
   cudaEventRecord(c->ev[7], c->stream);
+  if (!loss_out) return RT_OK;
   RT_CUDA(cudaMemcpyAsync(c->h_loss, c->d_loss, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss d2h");
   if ((rc = wait_stream(c))) return rc;
-  if (loss_out) *loss_out = c->h_loss[0];
+  *loss_out = c->h_loss[0];
   if (!std::isfinite(c->h_loss[0])) return set_err(c, RT_ERR_NONFINITE, "loss is not finite");
+  return RT_OK;
+}
+
+RT_API int rt_train_step(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets, int batch, uint32_t step,
+                         const rt_train_config* tc, float* loss_out) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (!tokens || !targets || !tc) return set_err(c, RT_ERR_ARG, "null argument");
+  if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
+  cudaSetDevice(c->device);
+  if ((rc = upload_tokens(c, c->io, tokens, targets, batch))) return rc;
+  float loss = 0.f;
+  if ((rc = train_step_device(c, c->io, step, tc, &loss))) return rc;
+  if (loss_out) *loss_out = loss;
+  return RT_OK;
+}
+
+RT_API int rt_stage_batch(rt_ctx* c, int slot, const uint32_t* tokens, const uint32_t* targets, int batch) {
+  if (!c || !tokens || !targets || slot < 0 || slot > 4095) return RT_ERR_ARG;
+  if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
+  cudaSetDevice(c->device);
+  if (static_cast<size_t>(slot) >= c->staged.size()) c->staged.resize(slot + 1);
+  rt::TokenBatch& tb = c->staged[slot];
+  if (!tb.tokens) {
+    alloc_token_batch(c, tb);
+    if (!tb.tokens || !tb.targets || !tb.perm || !tb.seg_start || !tb.seg_tok)
+      return set_err(c, RT_ERR_OOM, "staged batch allocation");
+  }
+  int rc;
+  if ((rc = upload_tokens(c, tb, tokens, targets, batch))) return rc;
+  RT_CUDA(cudaStreamSynchronize(c->stream), "stage sync");
+  return RT_OK;
+}
+
+RT_API int rt_train_step_staged(rt_ctx* c, int slot, uint32_t step, const rt_train_config* tc, float* loss_out) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (!tc || slot < 0 || static_cast<size_t>(slot) >= c->staged.size() || !c->staged[slot].tokens ||
+      c->staged[slot].batch == 0)
+    return set_err(c, RT_ERR_ARG, "no staged batch in that slot");
+  cudaSetDevice(c->device);
+  return train_step_device(c, c->staged[slot], step, tc, loss_out);
+}
+
+RT_API int rt_forward_staged(rt_ctx* c, int slot, float softcap) {
+  if (!c || slot < 0 || static_cast<size_t>(slot) >= c->staged.size() || c->staged[slot].batch == 0)
+    return RT_ERR_ARG;
+  cudaSetDevice(c->device);
+  c->cur = &c->staged[slot];
+  return forward_impl(c, c->staged[slot].batch, softcap);
+}
+
+RT_API int rt_sync(rt_ctx* c, float* loss_out) {
+  if (!c) return RT_ERR_ARG;
+  cudaSetDevice(c->device);
+  int rc;
+  if (loss_out) RT_CUDA(cudaMemcpyAsync(c->h_loss, c->d_loss, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss");
+  if ((rc = wait_stream(c))) return rc;
+  if (loss_out) *loss_out = c->h_loss[0];
+  return RT_OK;
+}
+
+RT_API int rt_ctx_stream(const rt_ctx* c, void** stream_out) {
+  if (!c || !stream_out) return RT_ERR_ARG;
+  *stream_out = c->stream;
+  return RT_OK;
+}
+
+RT_API int rt_last_h2d_bytes(const rt_ctx* c, int64_t* out) {
+  if (!c || !out) return RT_ERR_ARG;
+  *out = c->h2d_bytes_last;
   return RT_OK;
 }
 

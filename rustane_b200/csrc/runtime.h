@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <deque>
 #include <string>
 #include <vector>
 
@@ -43,6 +44,18 @@ struct KernelEvent {
 };
 
 struct NcclState;
+
+// One batch of token ids on the device plus the embedding-scatter segments
+// (positions grouped by token, ascending) built from it on the host.
+struct TokenBatch {
+  uint32_t* tokens = nullptr;
+  uint32_t* targets = nullptr;
+  int32_t* perm = nullptr;
+  int32_t* seg_start = nullptr;
+  uint32_t* seg_tok = nullptr;
+  int nseg = 0;
+  int batch = 0;
+};
 
 }  // namespace rt
 
@@ -91,13 +104,11 @@ struct rt_ctx {
   float* dvec = nullptr;     // [B, heads, S]
   float* dgamma_part = nullptr;
 
-  // tokens and the embedding-scatter segments
-  uint32_t* d_tokens = nullptr;
-  uint32_t* d_targets = nullptr;
-  int32_t* d_perm = nullptr;
-  int32_t* d_seg_start = nullptr;
-  uint32_t* d_seg_tok = nullptr;
-  int nseg = 0;
+  // tokens and the embedding-scatter segments: `io` is refilled by every call
+  // that takes host tokens; `staged` slots hold batches uploaded ahead of time.
+  rt::TokenBatch io;
+  std::deque<rt::TokenBatch> staged;  // deque: growing keeps `cur` valid
+  const rt::TokenBatch* cur = nullptr;  // batch used by the last / running forward
   void* h_stage = nullptr;  // pinned staging for token uploads
   size_t h_stage_bytes = 0;
   float* h_loss = nullptr;  // pinned
@@ -114,6 +125,7 @@ struct rt_ctx {
   bool grads_zero_pending = true;
   float last_softcap = 0.f;
   int64_t device_bytes = 0;
+  int64_t h2d_bytes_last = 0;
   std::vector<void*> allocations;
 
   // distributed
