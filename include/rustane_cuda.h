@@ -238,6 +238,20 @@ RT_API int rt_kernel_attention_bwd(const void* qkv, const void* out, const float
                                    float* dvec, void* dqkv, const float* rope_cos_b, const float* rope_sin_b,
                                    int batch, int seq, int heads, void* stream);
 
+/* Allocation-free variant of rt_kernel_attention_bwd, for callers that cannot
+ * call cudaMalloc when they run the backward pass (device memory owned by
+ * another allocator, or a loop that must not take cudaMalloc's implicit device
+ * synchronisation).  No counterpart in the reference: it has no GPU path.  The
+ * rowsum(dO * O) scratch comes from a 2 MiB array compiled into the library
+ * (held by every GPU that loads it until exit) instead of the caller:
+ * batch * heads * seq must be <= 524288, otherwise RT_ERR_SHAPE.  The first call
+ * on a device looks up that array's device address (make it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU race, so
+ * order them on one stream.  Inputs and outputs as rt_kernel_attention_bwd. */
+RT_API int rt_kernel_attention_bwd_noalloc(const void* qkv, const void* out, const float* lse2, const void* dout,
+                                           void* dqkv, const float* rope_cos_b, const float* rope_sin_b, int batch,
+                                           int seq, int heads, void* stream);
+
 /* Row RMSNorm over x [M, D] fp32 -> out bf16, rms_inv [M]
  * (cpu/rmsnorm.rs:149-183, token-major). */
 RT_API int rt_kernel_rmsnorm_fwd(const float* x, const float* gamma, void* out_bf16, float* rms_inv, int M, int D,
