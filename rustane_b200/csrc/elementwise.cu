@@ -101,90 +101,91 @@ __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __r
   }
 }
 
-constexpr int kBwdRows = 16;   // rows per block (dgamma partial granularity)
-constexpr int kBwdThreads = 256;
-constexpr int kBwdVec = 8;     // float4 per thread -> D <= 8192
-
-__global__ void __launch_bounds__(kBwdThreads)
-    rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
-                       const float* __restrict__ rms_inv, const float* __restrict__ resid, float* __restrict__ dx,
-                       __nv_bfloat16* __restrict__ dx_bf16, float bf16_scale, float* __restrict__ dgamma_part, int M,
-                       int D) {
-  __shared__ float red[32];
+// RMSNorm backward, row part: one warp per token row, two passes over the row
+// (the second pass re-reads dy and x from L1/L2).  dgamma is computed by the
+// column kernels below, so this kernel is a pure stream.
+__global__ void __launch_bounds__(256)
+    rmsnorm_bwd_rows_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
+                            const float* __restrict__ rms_inv, const float* __restrict__ resid, float* __restrict__ dx,
+                            __nv_bfloat16* __restrict__ dx_bf16, float bf16_scale, int M, int D) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
   const int D4 = D >> 2;
-  const int tid = threadIdx.x;
-  float4 g[kBwdVec], dga[kBwdVec];
-#pragma unroll
-  for (int j = 0; j < kBwdVec; ++j) {
-    const int c = tid + j * kBwdThreads;
-    g[j] = c < D4 ? reinterpret_cast<const float4*>(gamma)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-    dga[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t off = static_cast<int64_t>(row) * D;
+  const float4* dyr = reinterpret_cast<const float4*>(dy + off);
+  const float4* xr = reinterpret_cast<const float4*>(x + off);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float r = rms_inv[row];
+  float dot = 0.f;
+  for (int c = lane; c < D4; c += 32) {
+    const float4 a = dyr[c], b = xr[c], g = g4[c];
+    dot += a.x * g.x * (b.x * r) + a.y * g.y * (b.y * r) + a.z * g.z * (b.z * r) + a.w * g.w * (b.w * r);
   }
-  const float inv_dim = 1.0f / static_cast<float>(D);
-  const int m0 = blockIdx.x * kBwdRows;
-  for (int m = m0; m < m0 + kBwdRows && m < M; ++m) {
-    const float r = rms_inv[m];
-    const float4* dyr = reinterpret_cast<const float4*>(dy + static_cast<int64_t>(m) * D);
-    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(m) * D);
-    float4 dyv[kBwdVec], xh[kBwdVec];
-    float dot = 0.f;
-#pragma unroll
-    for (int j = 0; j < kBwdVec; ++j) {
-      const int c = tid + j * kBwdThreads;
-      if (c < D4) {
-        dyv[j] = dyr[c];
-        const float4 xv = xr[c];
-        xh[j] = make_float4(xv.x * r, xv.y * r, xv.z * r, xv.w * r);
-        dot += dyv[j].x * g[j].x * xh[j].x + dyv[j].y * g[j].y * xh[j].y + dyv[j].z * g[j].z * xh[j].z +
-               dyv[j].w * g[j].w * xh[j].w;
-      }
+  dot = warp_sum(dot) * (1.0f / static_cast<float>(D));
+  float4* o = reinterpret_cast<float4*>(dx + off);
+  const float4* rr = resid ? reinterpret_cast<const float4*>(resid + off) : nullptr;
+  uint2* ob = dx_bf16 ? reinterpret_cast<uint2*>(dx_bf16 + off) : nullptr;
+  for (int c = lane; c < D4; c += 32) {
+    const float4 a = dyr[c], b = xr[c], g = g4[c];
+    float4 v;  // dx = rms_inv * (dy*gamma - xhat * dot)   (cpu/rmsnorm.rs:229-236)
+    v.x = r * (a.x * g.x - (b.x * r) * dot);
+    v.y = r * (a.y * g.y - (b.y * r) * dot);
+    v.z = r * (a.z * g.z - (b.z * r) * dot);
+    v.w = r * (a.w * g.w - (b.w * r) * dot);
+    if (rr) {
+      const float4 q = rr[c];
+      v.x += q.x;
+      v.y += q.y;
+      v.z += q.z;
+      v.w += q.w;
     }
-    dot = block_sum(dot, red) * inv_dim;
-    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<int64_t>(m) * D);
-    const float4* rr = resid ? reinterpret_cast<const float4*>(resid + static_cast<int64_t>(m) * D) : nullptr;
-    uint2* ob = dx_bf16 ? reinterpret_cast<uint2*>(dx_bf16 + static_cast<int64_t>(m) * D) : nullptr;
-#pragma unroll
-    for (int j = 0; j < kBwdVec; ++j) {
-      const int c = tid + j * kBwdThreads;
-      if (c < D4) {
-        float4 o;
-        o.x = r * (dyv[j].x * g[j].x - xh[j].x * dot);
-        o.y = r * (dyv[j].y * g[j].y - xh[j].y * dot);
-        o.z = r * (dyv[j].z * g[j].z - xh[j].z * dot);
-        o.w = r * (dyv[j].w * g[j].w - xh[j].w * dot);
-        if (rr) {
-          const float4 q = rr[c];
-          o.x += q.x;
-          o.y += q.y;
-          o.z += q.z;
-          o.w += q.w;
-        }
-        dxr[c] = o;
-        if (ob)
-          ob[c] = make_uint2(pack_bf16x2(o.x * bf16_scale, o.y * bf16_scale),
-                             pack_bf16x2(o.z * bf16_scale, o.w * bf16_scale));
-        dga[j].x += dyv[j].x * xh[j].x;
-        dga[j].y += dyv[j].y * xh[j].y;
-        dga[j].z += dyv[j].z * xh[j].z;
-        dga[j].w += dyv[j].w * xh[j].w;
-      }
-    }
-  }
-  float4* part = reinterpret_cast<float4*>(dgamma_part + static_cast<int64_t>(blockIdx.x) * D);
-#pragma unroll
-  for (int j = 0; j < kBwdVec; ++j) {
-    const int c = tid + j * kBwdThreads;
-    if (c < D4) part[c] = dga[j];
+    o[c] = v;
+    if (ob)
+      ob[c] = make_uint2(pack_bf16x2(v.x * bf16_scale, v.y * bf16_scale), pack_bf16x2(v.z * bf16_scale, v.w * bf16_scale));
   }
 }
 
-__global__ void dgamma_reduce_kernel(const float* __restrict__ part, int nblk, float* __restrict__ dgamma, int D,
-                                     int accumulate) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+// dgamma column partials: part[chunk][d] = sum over rows of the chunk (ascending)
+// of dy[m,d] * x[m,d] * rms_inv[m]; a warp reads 32 consecutive columns of a row.
+constexpr int kDgRows = 64;
+__global__ void __launch_bounds__(256)
+    rmsnorm_dgamma_part_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                               const float* __restrict__ rms_inv, float* __restrict__ part, int M, int D) {
+  __shared__ float rs[kDgRows];
+  const int d = blockIdx.x * 256 + threadIdx.x;
+  const int m0 = blockIdx.y * kDgRows;
+  const int m1 = min(M, m0 + kDgRows);
+  if (threadIdx.x < kDgRows && m0 + threadIdx.x < M) rs[threadIdx.x] = rms_inv[m0 + threadIdx.x];
+  __syncthreads();
   if (d >= D) return;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int m = m0; m < m1; ++m) {
+    const int64_t i = static_cast<int64_t>(m) * D + d;
+    acc += dy[i] * (x[i] * rs[m - m0]);
+  }
+  part[static_cast<int64_t>(blockIdx.y) * D + d] = acc;
+}
+
+// dgamma[d] = (accumulate ? dgamma[d] : 0) + sum_b part[b][d]: 32 columns per block,
+// warp w sums partials w, w+8, ... in order, then the 8 warp sums in order.
+__global__ void __launch_bounds__(256) dgamma_reduce_kernel(const float* __restrict__ part, int nblk,
+                                                            float* __restrict__ dgamma, int D, int accumulate) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int d = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int b = 0; b < nblk; ++b) s += part[static_cast<int64_t>(b) * D + d];
-  dgamma[d] = accumulate ? dgamma[d] + s : s;
+  if (d < D)
+    for (int b = warp; b < nblk; b += 8) s += part[static_cast<int64_t>(b) * D + d];
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && d < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][lane];
+    dgamma[d] = accumulate ? dgamma[d] + t : t;
+  }
 }
 
 // --------------------------------------------------------- cross-entropy
@@ -448,17 +449,20 @@ int rmsnorm_fwd(const float* x, const float* gamma, __nv_bfloat16* out, float* r
   rmsnorm_fwd_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, gamma, out, rms_inv, M, D);
   return cudaGetLastError();
 }
-int rmsnorm_bwd_blocks(int M) { return (M + kBwdRows - 1) / kBwdRows; }
+int rmsnorm_bwd_blocks(int M) { return (M + kDgRows - 1) / kDgRows; }
 int rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float* rms_inv, const float* resid,
                 float* dx, __nv_bfloat16* dx_bf16, float bf16_scale, float* dgamma_part, int M, int D,
                 cudaStream_t s) {
-  if (D % 4 || D > 4 * kBwdThreads * kBwdVec) return -1;
-  rmsnorm_bwd_kernel<<<rmsnorm_bwd_blocks(M), kBwdThreads, 0, s>>>(dy, x, gamma, rms_inv, resid, dx, dx_bf16,
-                                                                   bf16_scale, dgamma_part, M, D);
+  if (D % 4) return -1;
+  // dgamma partials first: they read dy and x, which dx may alias
+  dim3 g2((D + 255) / 256, rmsnorm_bwd_blocks(M));
+  rmsnorm_dgamma_part_kernel<<<g2, 256, 0, s>>>(dy, x, rms_inv, dgamma_part, M, D);
+  rmsnorm_bwd_rows_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale,
+                                                               M, D);
   return cudaGetLastError();
 }
 int dgamma_reduce(const float* part, int nblk, float* dgamma, int D, int accumulate, cudaStream_t s) {
-  dgamma_reduce_kernel<<<(D + 255) / 256, 256, 0, s>>>(part, nblk, dgamma, D, accumulate);
+  dgamma_reduce_kernel<<<(D + 31) / 32, 256, 0, s>>>(part, nblk, dgamma, D, accumulate);
   return cudaGetLastError();
 }
 int ce_forward(const float* logits, const uint32_t* tgt, float* row_loss, float* row_lse, int M, int V,

@@ -13,9 +13,12 @@
 // Kernel organisation (one CTA per SM, persistent over output tiles):
 //   warp 0      : TMA producer (one lane) -> STAGES-deep smem ring
 //   warp 1      : MMA issuer  (one lane)  -> tcgen05.mma, 128 x BN x 16 per instruction
-//   warp 2      : TMEM allocator (2 x BN fp32 columns: double-buffered accumulator)
-//   warps 4..7  : epilogue, thread t owns accumulator row t (TMEM lane t)
-// The epilogue of tile i overlaps the MMAs of tile i+1.
+//   warp 2      : TMEM allocator (2 accumulator buffers of BN fp32 columns)
+//   warps 4..11 : epilogue; warp w reads TMEM lanes 32*(w%4).. (accumulator rows)
+//                 and one half of the tile's 32-column chunks, prefetching the
+//                 next chunk's auxiliary input (residual, h1|h3, old gradient)
+// The epilogue of tile i overlaps the MMAs of tile i+1.  Tile widths BN = 128,
+// 192 or 256 are chosen per shape from a wave-count cost model.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -29,13 +32,17 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 B = one swizzle row
 
+constexpr int kEpiWarps = 8;                    // warps 4..11: two per TMEM lane quadrant
+constexpr int kThreads = 128 + 32 * kEpiWarps;  // + producer, MMA, allocator, spare
+
 template <int BN>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 192 ? 5 : 6);
+  static constexpr int ACC_STRIDE = (BN == 192) ? 256 : BN;  // TMEM columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_STRIDE;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
@@ -86,16 +93,137 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
   }
 }
 
-// Epilogue of one 128 x BN accumulator tile for accumulator row m.
+// Per-chunk auxiliary inputs of the epilogue (loaded one chunk ahead so their
+// global-memory latency overlaps the previous chunk's work).
+struct AuxRegs {
+  uint4 u[8];
+};
+
+template <int EPI>
+__device__ __forceinline__ void load_aux(const KParams& p, int64_t mrow, int n, bool ok, AuxRegs& a) {
+  if (!ok) return;
+  if constexpr (EPI == kEpiResidual) {
+    const uint4* r = reinterpret_cast<const uint4*>(static_cast<const float*>(p.aux) + mrow * p.ld_aux + n);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) a.u[q] = r[q];
+  } else if constexpr (EPI == kEpiSwigluBwd) {
+    const __nv_bfloat16* h13 = static_cast<const __nv_bfloat16*>(p.aux) + mrow * p.ld_aux;
+    const uint4* h1 = reinterpret_cast<const uint4*>(h13 + n);
+    const uint4* h3 = reinterpret_cast<const uint4*>(h13 + p.n_half + n);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      a.u[q] = h1[q];
+      a.u[4 + q] = h3[q];
+    }
+  } else if constexpr (EPI == kEpiF32Acc) {
+    if (p.beta) {
+      const uint4* r = reinterpret_cast<const uint4*>(static_cast<const float*>(p.out) + mrow * p.ldo + n);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) a.u[q] = r[q];
+    }
+  }
+}
+
+__device__ __forceinline__ void unpack_bf16x32(const uint4* u, float* v) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    v[8 * q + 0] = bf16lo(u[q].x);
+    v[8 * q + 1] = bf16hi(u[q].x);
+    v[8 * q + 2] = bf16lo(u[q].y);
+    v[8 * q + 3] = bf16hi(u[q].y);
+    v[8 * q + 4] = bf16lo(u[q].z);
+    v[8 * q + 5] = bf16hi(u[q].z);
+    v[8 * q + 6] = bf16lo(u[q].w);
+    v[8 * q + 7] = bf16hi(u[q].w);
+  }
+}
+
+// One 32-column chunk of the epilogue for accumulator row m (values v[32] are fp32 accumulators).
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const KParams& p, int64_t mrow, int n, float* v, const AuxRegs& a) {
+  if constexpr (EPI == kEpiBf16) {
+    store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
+  } else if constexpr (EPI == kEpiF32 || EPI == kEpiF32Acc || EPI == kEpiResidual) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + mrow * p.ldo + n);
+    if constexpr (EPI == kEpiF32Acc) {
+      if (p.beta) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 o = *reinterpret_cast<const float4*>(&a.u[q]);
+          v[4 * q + 0] += o.x;
+          v[4 * q + 1] += o.y;
+          v[4 * q + 2] += o.z;
+          v[4 * q + 3] += o.w;
+        }
+      }
+    }
+    if constexpr (EPI == kEpiResidual) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 o = *reinterpret_cast<const float4*>(&a.u[q]);
+        v[4 * q + 0] = o.x + p.alpha * v[4 * q + 0];
+        v[4 * q + 1] = o.y + p.alpha * v[4 * q + 1];
+        v[4 * q + 2] = o.z + p.alpha * v[4 * q + 2];
+        v[4 * q + 3] = o.w + p.alpha * v[4 * q + 3];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else if constexpr (EPI == kEpiRope) {
+    // Interleaved-pair rotation per head of 128 (kernels/sdpa_fwd.rs:18-33, 100-128):
+    //   y[2i] = x[2i] cos - x[2i+1] sin,  y[2i+1] = x[2i+1] cos + x[2i] sin
+    if (n < p.rope_cols) {
+      const int pos = static_cast<int>(mrow % p.seq);
+      const int i0 = (n & 127) >> 1;
+      const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + pos * 64 + i0);
+      const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + pos * 64 + i0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 c4 = cs[q], s4 = sn[q];
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = 4 * q + e;
+          const float x0 = v[2 * t], x1 = v[2 * t + 1];
+          v[2 * t] = x0 * cc[e] - x1 * ss[e];
+          v[2 * t + 1] = x1 * cc[e] + x0 * ss[e];
+        }
+      }
+    }
+    store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
+  } else if constexpr (EPI == kEpiSwigluBwd) {
+    // C = dgate = dffn * W2 (layer.rs:1627-1641); SiLU-gate backward
+    // (layer.rs:1660-1666): dh3 = dg * silu(h1); dh1 = dg * h3 * sig * (1 + h1 (1 - sig)).
+    float h1[32], h3[32], dh1[32], dh3[32];
+    unpack_bf16x32(&a.u[0], h1);
+    unpack_bf16x32(&a.u[4], h3);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float sig;
+      const float sl = silu_sigmoid(h1[i], sig);
+      const float deriv = sig * (1.f + h1[i] * (1.f - sig));
+      dh3[i] = v[i] * sl;
+      dh1[i] = v[i] * h3[i] * deriv;
+    }
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo;
+    store_bf16x32(o + n, dh1);
+    store_bf16x32(o + p.n_half + n, dh3);
+  }
+}
+
+// Epilogue of this warp's share of one 128 x BN accumulator tile: accumulator
+// row m, 32-column chunks [c0, c1).  `pre` holds chunk c0's auxiliary inputs.
 template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, int m, int tn) {
+__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, int m, int tn, int c0, int c1,
+                                              AuxRegs& pre) {
   const bool row_ok = m < p.M;
+  const int64_t mrow = static_cast<int64_t>(m);
   if constexpr (EPI == kEpiSwiglu) {
     // Columns [0, BN/2) hold h1 = x W1, [BN/2, BN) hold h3 = x W3 for the
-    // same BN/2 hidden units (layer.rs / ffn_fused.rs:46-63 semantics).
+    // same BN/2 hidden units (kernels/ffn_fused.rs:46-63 semantics).
     constexpr int HALF = BN / 2;
 #pragma unroll 1
-    for (int c = 0; c < HALF / 32; ++c) {
+    for (int c = c0; c < c1; ++c) {
       uint32_t g[32], u[32];
       tmem_ld32(tbase + c * 32, g);
       tmem_ld32(tbase + HALF + c * 32, u);
@@ -110,97 +238,35 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, 
           float sig;
           gate[i] = silu_sigmoid(h1[i], sig) * h3[i];
         }
-        __nv_bfloat16* h13 = static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(m) * p.ldo;
+        __nv_bfloat16* h13 = static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo;
         store_bf16x32(h13 + j, h1);
         store_bf16x32(h13 + p.n_half + j, h3);
-        store_bf16x32(static_cast<__nv_bfloat16*>(p.out2) + static_cast<int64_t>(m) * p.ldo2 + j, gate);
+        store_bf16x32(static_cast<__nv_bfloat16*>(p.out2) + mrow * p.ldo2 + j, gate);
       }
     }
   } else {
+    AuxRegs cur = pre;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = c0; c < c1; ++c) {
+      const int n = tn * BN + c * 32;
+      AuxRegs nxt;
+      if (c + 1 < c1) load_aux<EPI>(p, mrow, n + 32, row_ok && n + 32 < p.N, nxt);
       uint32_t r[32];
       tmem_ld32(tbase + c * 32, r);
       tmem_ld_wait();
-      const int n = tn * BN + c * 32;
-      if (!row_ok || n >= p.N) continue;
-      float v[32];
+      if (row_ok && n < p.N) {
+        float v[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-      const int64_t mrow = static_cast<int64_t>(m);
-      if constexpr (EPI == kEpiBf16) {
-        store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
-      } else if constexpr (EPI == kEpiF32 || EPI == kEpiF32Acc || EPI == kEpiResidual) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + mrow * p.ldo + n);
-        if constexpr (EPI == kEpiF32Acc) {
-          if (p.beta) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 o = dst[q];
-              v[4 * q + 0] += o.x;
-              v[4 * q + 1] += o.y;
-              v[4 * q + 2] += o.z;
-              v[4 * q + 3] += o.w;
-            }
-          }
-        }
-        if constexpr (EPI == kEpiResidual) {
-          const float4* res =
-              reinterpret_cast<const float4*>(static_cast<const float*>(p.aux) + mrow * p.ld_aux + n);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4 o = res[q];
-            v[4 * q + 0] = o.x + p.alpha * v[4 * q + 0];
-            v[4 * q + 1] = o.y + p.alpha * v[4 * q + 1];
-            v[4 * q + 2] = o.z + p.alpha * v[4 * q + 2];
-            v[4 * q + 3] = o.w + p.alpha * v[4 * q + 3];
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      } else if constexpr (EPI == kEpiRope) {
-        // Interleaved-pair rotation per head of 128 (kernels/sdpa_fwd.rs:18-33, 100-128):
-        //   y[2i] = x[2i] cos - x[2i+1] sin,  y[2i+1] = x[2i+1] cos + x[2i] sin
-        if (n < p.rope_cols) {
-          const int pos = m % p.seq;
-          const int i0 = (n & 127) >> 1;
-          const float* cs = p.rope_cos + pos * 64 + i0;
-          const float* sn = p.rope_sin + pos * 64 + i0;
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const float c = cs[t], s = sn[t];
-            const float x0 = v[2 * t], x1 = v[2 * t + 1];
-            v[2 * t] = x0 * c - x1 * s;
-            v[2 * t + 1] = x1 * c + x0 * s;
-          }
-        }
-        store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
-      } else if constexpr (EPI == kEpiSwigluBwd) {
-        // C = dgate = dffn * W2 (layer.rs:1627-1641); SiLU-gate backward
-        // (layer.rs:1660-1666): dh3 = dg * silu(h1); dh1 = dg * h3 * sig * (1 + h1 (1 - sig)).
-        const __nv_bfloat16* h13 = static_cast<const __nv_bfloat16*>(p.aux) + mrow * p.ld_aux;
-        float h1[32], h3[32];
-        load_bf16x32(h13 + n, h1);
-        load_bf16x32(h13 + p.n_half + n, h3);
-        float dh1[32], dh3[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float sig;
-          const float s = silu_sigmoid(h1[i], sig);
-          const float deriv = sig * (1.f + h1[i] * (1.f - sig));
-          dh3[i] = v[i] * s;
-          dh1[i] = v[i] * h3[i] * deriv;
-        }
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo;
-        store_bf16x32(o + n, dh1);
-        store_bf16x32(o + p.n_half + n, dh3);
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        epilogue_chunk<EPI>(p, mrow, n, v, cur);
       }
+      cur = nxt;
     }
   }
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const KParams p) {
   using C = GemmCfg<BN>;
@@ -224,7 +290,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);
+      mbar_init(&tempty_bar[a], kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -312,7 +378,7 @@ __global__ void __launch_bounds__(256, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE);
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int stage = it % C::STAGES;
           const uint32_t phase = (it / C::STAGES) & 1;
@@ -343,11 +409,21 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
+    const int q = warp & 3;               // TMEM lane quadrant = accumulator rows 32q..32q+31
+    const int half = (warp - 4) >> 2;     // which half of the tile's 32-column chunks
+    constexpr int NCH = (EPI == kEpiSwiglu) ? (BN / 2) / 32 : BN / 32;
+    const int c0 = half * NCH / 2, c1 = (half + 1) * NCH / 2;
     int local = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (local >> 1) & 1;
+      const int tm = tile % p.num_m, tn = tile / p.num_m;
+      const int m = tm * BM + q * 32 + lane;
+      AuxRegs pre;  // first chunk's auxiliary inputs do not depend on the MMA: fetch before waiting
+      if constexpr (EPI != kEpiSwiglu) {
+        const int n0 = tn * BN + c0 * 32;
+        if (c0 < c1) load_aux<EPI>(p, static_cast<int64_t>(m), n0, m < p.M && n0 < p.N, pre);
+      }
       bool ok = mbar_wait(&tfull_bar[acc], acc_par);
       ok = __all_sync(0xffffffffu, ok);
       const int aborted = __shfl_sync(0xffffffffu, *abort_flag, 0);
@@ -359,10 +435,9 @@ __global__ void __launch_bounds__(256, 1)
         break;
       }
       tc_fence_after();
-      const int tm = tile % p.num_m, tn = tile / p.num_m;
-      const int m = tm * BM + q * 32 + lane;
-      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(p, tbase, m, tn);
+      const uint32_t tbase =
+          tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE) + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue_tile<BN, EPI>(p, tbase, m, tn, c0, c1, pre);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -410,7 +485,7 @@ int launch_inst(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
   static const cudaError_t attr = cudaFuncSetAttribute(gemm_tc_kernel<BN, A_MN, B_MN, EPI>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (attr != cudaSuccess) return attr;
-  gemm_tc_kernel<BN, A_MN, B_MN, EPI><<<grid, 256, C::SMEM_BYTES, s>>>(ta, tb, kp);
+  gemm_tc_kernel<BN, A_MN, B_MN, EPI><<<grid, kThreads, C::SMEM_BYTES, s>>>(ta, tb, kp);
   return cudaGetLastError();
 }
 
@@ -475,14 +550,22 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     return ((g.M + BM - 1) / BM) * ((g.N + per_tile_n - 1) / per_tile_n);
   };
   int bn = g.force_bn;
-  if (bn != 128 && bn != 256) {
-    // Prefer the wide tile unless it leaves noticeably more of the last wave idle.
-    const int t256 = tiles_for(256), t128 = tiles_for(128);
-    const double e256 = double(t256) / (double((t256 + sms - 1) / sms) * sms);
-    const double e128 = double(t128) / (double((t128 + sms - 1) / sms) * sms);
-    bn = (e256 >= 0.85 * e128) ? 256 : 128;
+  if (bn != 128 && bn != 192 && bn != 256) {
+    // time ~ waves x tile width / efficiency: 128-wide tiles are closer to the
+    // shared-memory read limit (A is re-read per 128 columns), 256 is the best.
+    double best = 1e30;
+    for (int cand : {256, 192, 128}) {
+      if (swiglu && (cand == 192 || g.N % (cand / 2) != 0)) continue;
+      const double eff = cand == 256 ? 1.0 : (cand == 192 ? 0.95 : 0.82);
+      const int t = tiles_for(cand);
+      const double cost = double((t + sms - 1) / sms) * cand / eff;
+      if (cost < best * 0.999) {
+        best = cost;
+        bn = cand;
+      }
+    }
   }
-  if (swiglu && (g.N % (bn / 2) != 0)) bn = 128;
+  if (swiglu && (bn == 192 || g.N % (bn / 2) != 0)) bn = 128;
 
   KParams kp{};
   kp.M = g.M;
@@ -521,7 +604,9 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (!ok) return -3;
 
   const int grid = kp.num_tiles < sms ? kp.num_tiles : sms;
-  return bn == 256 ? dispatch<256>(g, ta, tb, kp, grid, stream) : dispatch<128>(g, ta, tb, kp, grid, stream);
+  if (bn == 256) return dispatch<256>(g, ta, tb, kp, grid, stream);
+  if (bn == 192) return dispatch<192>(g, ta, tb, kp, grid, stream);
+  return dispatch<128>(g, ta, tb, kp, grid, stream);
 }
 
 }  // namespace rt

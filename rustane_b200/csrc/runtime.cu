@@ -504,7 +504,7 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
     if ((rc = gemm(c, g, "dE"))) return rc;
   }
   // final RMSNorm backward (full_model.rs:315-318); also alpha*dy for the last layer
-  RT_OTHER(1, rt::rmsnorm_bwd(c->dx_tmp, c->x_out, P + c->off_gamma_final, c->rms_f, nullptr, c->dy_a, c->dffn, alpha,
+  RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, c->x_out, P + c->off_gamma_final, c->rms_f, nullptr, c->dy_a, c->dffn, alpha,
                               c->dgamma_part, M, D, c->stream),
            "final rmsnorm bwd");
   RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + c->off_gamma_final, D, beta, c->stream), "dgamma");
@@ -546,7 +546,7 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
       if ((rc = gemm(c, g, "dW13"))) return rc;
     }
     // RMSNorm2 backward + dy (layer.rs:1702-1706); dx2s = alpha * dx2
-    RT_OTHER(1, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s, alpha, c->dgamma_part, M,
+    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s, alpha, c->dgamma_part, M,
                                 D, c->stream),
              "rmsnorm2 bwd");
     RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma2, D, beta, c->stream), "dgamma2");
@@ -592,7 +592,7 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
       if ((rc = gemm(c, g, "dWqkv"))) return rc;
     }
     // RMSNorm1 backward + dx2 (layer.rs:1853-1857); alpha * dx for the layer below
-    RT_OTHER(1, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next, l > 0 ? c->dffn : nullptr,
+    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next, l > 0 ? c->dffn : nullptr,
                                 alpha, c->dgamma_part, M, D, c->stream),
              "rmsnorm1 bwd");
     RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma1, D, beta, c->stream), "dgamma1");
