@@ -1,0 +1,84 @@
+"""Data-parallel train step on 2 GPUs through the C ABI (rt_dist_init + NCCL
+all-reduce inside rt_train_step): two ranks with one sequence each must match
+one GPU stepping on both sequences.  Skipped on boxes with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(dim=256, hidden=512, heads=2, nlayers=2, seq=128, vocab=512)
+
+
+def _cfg():
+    from rustane_b200.model import ModelConfig
+    return ModelConfig.custom(CFG["dim"], CFG["hidden"], CFG["heads"], CFG["nlayers"], seq=CFG["seq"],
+                              vocab=CFG["vocab"])
+
+
+def _data():
+    rng = np.random.default_rng(31)
+    n = 2 * CFG["seq"]
+    return rng.integers(0, CFG["vocab"], n).astype(np.uint32), rng.integers(0, CFG["vocab"], n).astype(np.uint32)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, out):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    sys.path[:0] = [str(root)]
+    from rustane_b200 import CompiledKernels, TrainConfig
+    from rustane_b200.tensors import ModelTensors
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = _cfg()
+        k = CompiledKernels.compile(cfg, max_batch=1, device=rank)
+        k.upload_weights(ModelTensors.normal(cfg, seed=3, std=0.02))
+        uid = [CompiledKernels.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        k.dist_init(world, rank, uid[0], timeout_ms=60000)
+        tok, tgt = _data()
+        S = cfg.seq
+        tc = TrainConfig(warmup_steps=2, total_steps=10)
+        losses = [k.train_step(tok[rank * S:(rank + 1) * S], tgt[rank * S:(rank + 1) * S], s, tc) for s in range(2)]
+        w = k.download_weights()
+        if rank == 0:
+            np.savez(out, losses=np.array(losses), **{n: a for n, a in w.tensors()})
+        k.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_dp2_matches_single_gpu(tmp_path):
+    from rustane_b200 import CompiledKernels, TrainConfig
+    from rustane_b200.tensors import ModelTensors
+    out = str(tmp_path / "dp.npz")
+    mp.spawn(_rank, args=(2, _free_port(), out), nprocs=2, join=True)
+    got = np.load(out)
+    cfg = _cfg()
+    k = CompiledKernels.compile(cfg, max_batch=2, device=0)
+    k.upload_weights(ModelTensors.normal(cfg, seed=3, std=0.02))
+    tok, tgt = _data()
+    tc = TrainConfig(warmup_steps=2, total_steps=10)
+    for s in range(2):
+        k.train_step(tok, tgt, s, tc)
+    w = k.download_weights()
+    for name, a in w.tensors():
+        b = got[name]
+        # same math, different GEMM summation order over the two sequences
+        assert np.max(np.abs(a - b)) <= 1e-4 * max(np.max(np.abs(a)), 1e-3) + 2e-6, name
