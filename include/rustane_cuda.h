@@ -96,7 +96,7 @@ typedef struct rt_model_ptrs {
 
 /* Device-side phase and kernel timings (CUDA events on the context stream). */
 typedef struct rt_timings {
-  double fwd_ms, bwd_ms, comm_ms, opt_ms; /* last forward / backward / all-reduce / norm+AdamW */
+  double fwd_ms, bwd_ms, comm_ms, opt_ms; /* last forward / backward / all-reduce span / norm+AdamW */
   double gemm_ms, gemm_flops;             /* accumulated over GEMM launches while profiling   */
   double attn_ms, attn_flops;             /* accumulated over attention launches              */
   double other_ms;                        /* accumulated over all other kernels               */

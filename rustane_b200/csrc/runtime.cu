@@ -121,16 +121,16 @@ cudaEvent_t pool_event(rt_ctx* c) {
 
 // Run one launcher, count its kernels and time it when profiling.
 template <class F>
-int launch(rt_ctx* c, int kind, double flops, int nkernels, F&& f) {
+int launch_on(rt_ctx* c, cudaStream_t st, int kind, double flops, int nkernels, F&& f) {
   cudaEvent_t a = nullptr, b = nullptr;
   if (c->profiling) {
     a = pool_event(c);
-    cudaEventRecord(a, c->stream);
+    cudaEventRecord(a, st);
   }
   const int rc = f();
   if (c->profiling) {
     b = pool_event(c);
-    cudaEventRecord(b, c->stream);
+    cudaEventRecord(b, st);
     c->kevents.push_back({kind, flops, a, b});
   }
   c->acc.kernel_launches += nkernels;
@@ -138,6 +138,10 @@ int launch(rt_ctx* c, int kind, double flops, int nkernels, F&& f) {
   else if (kind == 1) c->acc.attn_launches += nkernels;
   else c->acc.other_launches += nkernels;
   return rc;
+}
+template <class F>
+int launch(rt_ctx* c, int kind, double flops, int nkernels, F&& f) {
+  return launch_on(c, c->stream, kind, flops, nkernels, f);
 }
 
 void harvest_kernel_events(rt_ctx* c) {
@@ -158,11 +162,12 @@ void harvest_kernel_events(rt_ctx* c) {
   c->event_pool_used = 0;
 }
 
-int gemm(rt_ctx* c, rt::GemmArgs g, const char* what) {
+int gemm(rt_ctx* c, rt::GemmArgs g, const char* what, cudaStream_t st = nullptr) {
   g.err = c->d_err;
+  if (!st) st = c->stream;
   const double n_out = g.epi == rt::kEpiSwiglu ? 2.0 * g.N : double(g.N);
   const double fl = 2.0 * double(g.M) * n_out * double(g.K);
-  RT_LAUNCH(launch(c, 0, fl, 1, [&] { return rt::gemm_launch(g, c->stream); }), what);
+  RT_LAUNCH(launch_on(c, st, 0, fl, 1, [&] { return rt::gemm_launch(g, st); }), what);
   return RT_OK;
 }
 
@@ -465,6 +470,7 @@ int forward_impl(rt_ctx* c, int batch, float softcap) {
   RT_OTHER(1, rt::ce_forward(c->logits, c->cur->targets, c->row_loss, c->row_lse, M, V, softcap, c->stream), "ce fwd");
   RT_OTHER(1, rt::mean_reduce(c->row_loss, M, c->d_loss, c->stream), "loss mean");
   cudaEventRecord(c->ev[1], c->stream);
+  c->ev_recorded |= 1u;
   c->cur_batch = batch;
   c->fwd_done = true;
   c->last_softcap = softcap;
@@ -472,9 +478,25 @@ int forward_impl(rt_ctx* c, int batch, float softcap) {
 }
 
 // --------------------------------------------------------------- backward
+// Data-parallel all-reduce of one contiguous gradient range on the comm stream.
+int allreduce_range(rt_ctx* c, int64_t begin, int64_t end, cudaStream_t st) {
+  rt::NcclApi* api = rt::nccl_api();
+  if (!api || !c->nccl || !c->nccl->comm) return set_err(c, RT_ERR_NCCL, "no communicator (aborted or not initialised)");
+  ncclResult_t r = api->allReduce(c->grads + begin, c->grads + begin, static_cast<size_t>(end - begin), ncclFloat32,
+                                  ncclSum, c->nccl->comm, st);
+  if (r != ncclSuccess) return set_err(c, RT_ERR_NCCL, std::string("ncclAllReduce: ") + api->errorString(r));
+  return RT_OK;
+}
+
+// Backward of the last forward.  The data-gradient chain (dlogits -> dx of each
+// layer) runs on the main stream; each layer's four weight-gradient GEMMs run on
+// s_dw as soon as their inputs exist, reading parity-double-buffered
+// temporaries; with overlap_allreduce each layer's gradients are all-reduced on
+// s_comm right after its weight-gradient GEMMs.  On return the main stream has
+// waited for all of it.
 int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   const auto& cfg = c->cfg;
-  const int D = cfg.dim, H = cfg.hidden, V = cfg.vocab, S = cfg.seq;
+  const int D = cfg.dim, H = cfg.hidden, V = cfg.vocab, S = cfg.seq, L = cfg.nlayers;
   const int batch = c->cur_batch, M = batch * S;
   const float alpha = alpha_of(cfg);
   const int beta = c->grads_zero_pending ? 0 : 1;
@@ -482,11 +504,23 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   const float* P = c->params;
   float* Gr = c->grads;
   const int nblk = rt::rmsnorm_bwd_blocks(M);
+  cudaStream_t ms = c->stream, ds = c->s_dw;
   int rc;
-  cudaEventRecord(c->ev[2], c->stream);
+  cudaEventRecord(c->ev[2], ms);
   // dlogits * loss_scale (full_model.rs:265-276); CE mean over seq per sequence (cross_entropy.rs:92-95)
-  RT_OTHER(1, rt::ce_backward(c->logits, c->row_lse, c->cur->targets, c->dl, M, V, softcap, loss_scale / S, c->stream),
+  RT_OTHER(1, rt::ce_backward(c->logits, c->row_lse, c->cur->targets, c->dl, M, V, softcap, loss_scale / S, ms),
            "ce bwd");
+  cudaEventRecord(c->ev_ce, ms);
+  {  // dE += dl^T x_final   (full_model.rs:299-312) -- weight-gradient stream
+    cudaStreamWaitEvent(ds, c->ev_ce, 0);
+    rt::GemmArgs g;
+    g.a = c->dl; g.lda = V; g.a_mn = true;
+    g.b = c->xf; g.ldb = D; g.b_mn = true;
+    g.M = V; g.N = D; g.K = M;
+    g.epi = rt::kEpiF32Acc; g.out = Gr; g.ldo = D; g.beta = beta;
+    if ((rc = gemm(c, g, "dE", ds))) return rc;
+    cudaEventRecord(c->ev_de, ds);
+  }
   {  // dx_final = dl * E   (full_model.rs:279-289)
     rt::GemmArgs g;
     g.a = c->dl; g.lda = V;
@@ -495,113 +529,135 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
     g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
     if ((rc = gemm(c, g, "dx_final"))) return rc;
   }
-  {  // dE += dl^T x_final   (full_model.rs:299-312)
-    rt::GemmArgs g;
-    g.a = c->dl; g.lda = V; g.a_mn = true;
-    g.b = c->xf; g.ldb = D; g.b_mn = true;
-    g.M = V; g.N = D; g.K = M;
-    g.epi = rt::kEpiF32Acc; g.out = Gr; g.ldo = D; g.beta = beta;
-    if ((rc = gemm(c, g, "dE"))) return rc;
-  }
   // final RMSNorm backward (full_model.rs:315-318); also alpha*dy for the last layer
-  RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, c->x_out, P + c->off_gamma_final, c->rms_f, nullptr, c->dy_a, c->dffn, alpha,
-                              c->dgamma_part, M, D, c->stream),
+  RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, c->x_out, P + c->off_gamma_final, c->rms_f, nullptr, c->dy_a,
+                              c->dffn[(L - 1) & 1], alpha, c->dgamma_part, M, D, ms),
            "final rmsnorm bwd");
-  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + c->off_gamma_final, D, beta, c->stream), "dgamma");
+  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + c->off_gamma_final, D, beta, ms), "dgamma");
   float* dy = c->dy_a;
   float* dy_next = c->dy_b;
-  for (int l = cfg.nlayers - 1; l >= 0; --l) {
+  for (int l = L - 1; l >= 0; --l) {
     const rt::LayerActs& A = c->acts[l];
     const auto& o = c->layer_off[l];
+    const int p = l & 1;
+    // the parity-p temporaries were last read by the weight GEMMs of layer l + 2
+    if (l + 2 < L) cudaStreamWaitEvent(ms, c->ev_dw_done[l + 2], 0);
     {  // ffnBwdW2t + SiLU backward (layer.rs:1627-1667)
       rt::GemmArgs g;
-      g.a = c->dffn; g.lda = D;
+      g.a = c->dffn[p]; g.lda = D;
       g.b = W + o.w2; g.ldb = H; g.b_mn = true;
       g.M = M; g.N = H; g.K = D;
-      g.epi = rt::kEpiSwigluBwd; g.aux = A.h13; g.ld_aux = 2 * H; g.out = c->dh13; g.ldo = 2 * H; g.n_half = H;
+      g.epi = rt::kEpiSwigluBwd; g.aux = A.h13; g.ld_aux = 2 * H; g.out = c->dh13[p]; g.ldo = 2 * H; g.n_half = H;
       if ((rc = gemm(c, g, "dgate"))) return rc;
     }
+    cudaEventRecord(c->ev_dgate[l], ms);
+    cudaStreamWaitEvent(ds, c->ev_dgate[l], 0);
     {  // dW2 += dffn^T gate (layer.rs:1754)
       rt::GemmArgs g;
-      g.a = c->dffn; g.lda = D; g.a_mn = true;
+      g.a = c->dffn[p]; g.lda = D; g.a_mn = true;
       g.b = A.gate; g.ldb = H; g.b_mn = true;
       g.M = D; g.N = H; g.K = M;
       g.epi = rt::kEpiF32Acc; g.out = Gr + o.w2; g.ldo = H; g.beta = beta;
-      if ((rc = gemm(c, g, "dW2"))) return rc;
+      if ((rc = gemm(c, g, "dW2", ds))) return rc;
+    }
+    {  // dW1 | dW3 += x2norm^T (dh1 | dh3) (layer.rs:1692, 1787)
+      rt::GemmArgs g;
+      g.a = A.x2n; g.lda = D; g.a_mn = true;
+      g.b = c->dh13[p]; g.ldb = 2 * H; g.b_mn = true;
+      g.M = D; g.N = 2 * H; g.K = M;
+      g.epi = rt::kEpiF32Acc; g.out = Gr + o.w13; g.ldo = 2 * H; g.beta = beta;
+      if ((rc = gemm(c, g, "dW13", ds))) return rc;
     }
     {  // ffnBwdW13t: dx_ffn = dh1 W1^T + dh3 W3^T (layer.rs:1671-1699)
       rt::GemmArgs g;
-      g.a = c->dh13; g.lda = 2 * H;
+      g.a = c->dh13[p]; g.lda = 2 * H;
       g.b = W + o.w13; g.ldb = 2 * H; g.b_mn = false;
       g.M = M; g.N = D; g.K = 2 * H;
       g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
       if ((rc = gemm(c, g, "dx_ffn"))) return rc;
     }
-    {  // dW1 | dW3 += x2norm^T (dh1 | dh3) (layer.rs:1692, 1787)
-      rt::GemmArgs g;
-      g.a = A.x2n; g.lda = D; g.a_mn = true;
-      g.b = c->dh13; g.ldb = 2 * H; g.b_mn = true;
-      g.M = D; g.N = 2 * H; g.K = M;
-      g.epi = rt::kEpiF32Acc; g.out = Gr + o.w13; g.ldo = 2 * H; g.beta = beta;
-      if ((rc = gemm(c, g, "dW13"))) return rc;
-    }
     // RMSNorm2 backward + dy (layer.rs:1702-1706); dx2s = alpha * dx2
-    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s, alpha, c->dgamma_part, M,
-                                D, c->stream),
+    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s[p], alpha, c->dgamma_part,
+                                M, D, ms),
              "rmsnorm2 bwd");
-    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma2, D, beta, c->stream), "dgamma2");
+    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma2, D, beta, ms), "dgamma2");
+    cudaEventRecord(c->ev_rms2[l], ms);
+    cudaStreamWaitEvent(ds, c->ev_rms2[l], 0);
+    {  // dWo += attn^T dx2s (layer.rs:1753)
+      rt::GemmArgs g;
+      g.a = A.attn; g.lda = cfg.q_dim; g.a_mn = true;
+      g.b = c->dx2s[p]; g.ldb = D; g.b_mn = true;
+      g.M = cfg.q_dim; g.N = D; g.K = M;
+      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wo; g.ldo = D; g.beta = beta;
+      if ((rc = gemm(c, g, "dWo", ds))) return rc;
+    }
     {  // wotBwd: da = dx2s Wo^T (layer.rs:1709-1733)
       rt::GemmArgs g;
-      g.a = c->dx2s; g.lda = D;
+      g.a = c->dx2s[p]; g.lda = D;
       g.b = W + o.wo; g.ldb = D; g.b_mn = false;
       g.M = M; g.N = cfg.q_dim; g.K = D;
       g.epi = rt::kEpiBf16; g.out = c->da; g.ldo = cfg.q_dim;
       if ((rc = gemm(c, g, "da"))) return rc;
     }
-    {  // dWo += attn^T dx2s (layer.rs:1753)
-      rt::GemmArgs g;
-      g.a = A.attn; g.lda = cfg.q_dim; g.a_mn = true;
-      g.b = c->dx2s; g.ldb = D; g.b_mn = true;
-      g.M = cfg.q_dim; g.N = D; g.K = M;
-      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wo; g.ldo = D; g.beta = beta;
-      if ((rc = gemm(c, g, "dWo"))) return rc;
-    }
     {  // sdpaBwd1 + sdpaBwd2 + RoPE backward (layer.rs:1736-1798)
       rt::AttnArgs a;
       a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
       a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
-      a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv; a.lddq = 3 * D;
+      a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv[p]; a.lddq = 3 * D;
       a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b;
       const double fl = 2.5 * 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
-      RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward(a, c->stream); }), "attention bwd");
+      RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward(a, ms); }), "attention bwd");
+    }
+    cudaEventRecord(c->ev_attn[l], ms);
+    cudaStreamWaitEvent(ds, c->ev_attn[l], 0);
+    {  // dWq | dWk | dWv += xnorm^T (dq | dk | dv) (layer.rs:1838-1840)
+      rt::GemmArgs g;
+      g.a = A.xn; g.lda = D; g.a_mn = true;
+      g.b = c->dqkv[p]; g.ldb = 3 * D; g.b_mn = true;
+      g.M = D; g.N = 3 * D; g.K = M;
+      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wqkv; g.ldo = 3 * D; g.beta = beta;
+      if ((rc = gemm(c, g, "dWqkv", ds))) return rc;
+    }
+    cudaEventRecord(c->ev_dw_done[l], ds);
+    if (c->overlap_allreduce) {  // this layer's matrices are final: reduce them while backward continues
+      cudaStreamWaitEvent(c->s_comm, c->ev_dw_done[l], 0);
+      if (l == L - 1) cudaEventRecord(c->ev[4], c->s_comm);
+      if ((rc = allreduce_range(c, o.wqkv, o.w2 + int64_t(D) * H, c->s_comm))) return rc;
     }
     {  // qBwd + kvBwd: dx_attn = dq Wq^T + dk Wk^T + dv Wv^T (layer.rs:1800-1850)
       rt::GemmArgs g;
-      g.a = c->dqkv; g.lda = 3 * D;
+      g.a = c->dqkv[p]; g.lda = 3 * D;
       g.b = W + o.wqkv; g.ldb = 3 * D; g.b_mn = false;
       g.M = M; g.N = D; g.K = 3 * D;
       g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
       if ((rc = gemm(c, g, "dx_attn"))) return rc;
     }
-    {  // dWq | dWk | dWv += xnorm^T (dq | dk | dv) (layer.rs:1838-1840)
-      rt::GemmArgs g;
-      g.a = A.xn; g.lda = D; g.a_mn = true;
-      g.b = c->dqkv; g.ldb = 3 * D; g.b_mn = true;
-      g.M = D; g.N = 3 * D; g.K = M;
-      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wqkv; g.ldo = 3 * D; g.beta = beta;
-      if ((rc = gemm(c, g, "dWqkv"))) return rc;
-    }
-    // RMSNorm1 backward + dx2 (layer.rs:1853-1857); alpha * dx for the layer below
-    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next, l > 0 ? c->dffn : nullptr,
-                                alpha, c->dgamma_part, M, D, c->stream),
+    // RMSNorm1 backward + dx2 (layer.rs:1853-1857); alpha * dx for the layer below, into the
+    // other parity's dffn, last read by the weight GEMMs of layer l + 1
+    if (l > 0 && l + 1 < L) cudaStreamWaitEvent(ms, c->ev_dw_done[l + 1], 0);
+    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next,
+                                l > 0 ? c->dffn[(l - 1) & 1] : nullptr, alpha, c->dgamma_part, M, D, ms),
              "rmsnorm1 bwd");
-    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma1, D, beta, c->stream), "dgamma1");
+    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma1, D, beta, ms), "dgamma1");
     std::swap(dy, dy_next);
   }
-  // embedding scatter-add (full_model.rs:330)
-  RT_OTHER(1, rt::embed_scatter(dy, c->cur->perm, c->cur->seg_start, c->cur->seg_tok, c->cur->nseg, Gr, D, c->stream),
+  // embedding scatter-add (full_model.rs:330), after the dE GEMM
+  cudaStreamWaitEvent(ms, c->ev_de, 0);
+  RT_OTHER(1, rt::embed_scatter(dy, c->cur->perm, c->cur->seg_start, c->cur->seg_tok, c->cur->nseg, Gr, D, ms),
            "embed scatter");
-  cudaEventRecord(c->ev[3], c->stream);
+  cudaStreamWaitEvent(ms, c->ev_dw_done[0], 0);  // every weight gradient is final
+  if (c->overlap_allreduce) {  // last buckets: embedding and the gammas
+    cudaEventRecord(c->ev_main_done, ms);
+    cudaStreamWaitEvent(c->s_comm, c->ev_main_done, 0);
+    if ((rc = allreduce_range(c, 0, c->n_embed, c->s_comm))) return rc;
+    if ((rc = allreduce_range(c, c->n_matrix_end, c->n_params, c->s_comm))) return rc;
+    cudaEventRecord(c->ev[5], c->s_comm);
+    c->ev_recorded |= 4u;
+    cudaEventRecord(c->ev_comm_all, c->s_comm);
+    cudaStreamWaitEvent(ms, c->ev_comm_all, 0);
+  }
+  cudaEventRecord(c->ev[3], ms);
+  c->ev_recorded |= 2u;
   c->grads_zero_pending = false;
   return RT_OK;
 }
@@ -694,6 +750,15 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
   if (cudaSetDevice(device) != cudaSuccess) return bail(RT_ERR_CUDA, "cudaSetDevice");
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return bail(RT_ERR_CUDA, "stream");
   for (auto& e : c->ev) cudaEventCreate(&e);
+  if (cudaStreamCreateWithFlags(&c->s_dw, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&c->s_comm, cudaStreamNonBlocking) != cudaSuccess)
+    return bail(RT_ERR_CUDA, "streams");
+  for (auto* v : {&c->ev_dgate, &c->ev_rms2, &c->ev_attn, &c->ev_dw_done, &c->ev_comm}) {
+    v->resize(cfg.nlayers);
+    for (auto& e : *v) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+  }
+  for (cudaEvent_t* e : {&c->ev_ce, &c->ev_de, &c->ev_main_done, &c->ev_comm_all})
+    cudaEventCreateWithFlags(e, cudaEventDisableTiming);
 
   const int64_t D = cfg.dim, H = cfg.hidden, V = cfg.vocab, S = cfg.seq, L = cfg.nlayers, Q = cfg.q_dim;
   const int64_t M = int64_t(max_batch) * S;
@@ -781,15 +846,21 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
     c->dy_b = dalloc<float>(c, M * D);
     c->dx_tmp = dalloc<float>(c, M * D);
     c->dx2 = dalloc<float>(c, M * D);
-    c->dffn = dalloc<bf16>(c, M * D);
-    c->dx2s = dalloc<bf16>(c, M * D);
+    for (int p = 0; p < 2; ++p) {
+      c->dffn[p] = dalloc<bf16>(c, M * D);
+      c->dx2s[p] = dalloc<bf16>(c, M * D);
+      c->dh13[p] = dalloc<bf16>(c, M * 2 * H);
+      c->dqkv[p] = dalloc<bf16>(c, M * 3 * D);
+      need(c->dffn[p]);
+      need(c->dx2s[p]);
+      need(c->dh13[p]);
+      need(c->dqkv[p]);
+    }
     c->da = dalloc<bf16>(c, M * D);
-    c->dh13 = dalloc<bf16>(c, M * 2 * H);
-    c->dqkv = dalloc<bf16>(c, M * 3 * D);
     c->dvec = dalloc<float>(c, M * cfg.heads);
     c->dgamma_part = dalloc<float>(c, int64_t(rt::rmsnorm_bwd_blocks(static_cast<int>(M))) * D);
-    for (void* p : {(void*)c->dl, (void*)c->dy_b, (void*)c->dx_tmp, (void*)c->dx2, (void*)c->dffn, (void*)c->dx2s,
-                    (void*)c->da, (void*)c->dh13, (void*)c->dqkv, (void*)c->dvec, (void*)c->dgamma_part})
+    for (void* p : {(void*)c->dl, (void*)c->dy_b, (void*)c->dx_tmp, (void*)c->dx2, (void*)c->da, (void*)c->dvec,
+                    (void*)c->dgamma_part})
       need(p);
   }
   alloc_token_batch(c, c->io);
@@ -821,6 +892,8 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
 RT_API int rt_ctx_destroy(rt_ctx* c) {
   if (!c) return RT_ERR_ARG;
   if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->s_dw) cudaStreamSynchronize(c->s_dw);
+  if (c->s_comm) cudaStreamSynchronize(c->s_comm);
   if (c->nccl) {
     if (c->nccl->comm) {
       if (rt::NcclApi* api = rt::nccl_api()) api->commDestroy(c->nccl->comm);
@@ -833,6 +906,13 @@ RT_API int rt_ctx_destroy(rt_ctx* c) {
   for (auto& e : c->ev)
     if (e) cudaEventDestroy(e);
   for (auto e : c->event_pool) cudaEventDestroy(e);
+  for (auto* v : {&c->ev_dgate, &c->ev_rms2, &c->ev_attn, &c->ev_dw_done, &c->ev_comm})
+    for (auto e : *v)
+      if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : {c->ev_ce, c->ev_de, c->ev_main_done, c->ev_comm_all})
+    if (e) cudaEventDestroy(e);
+  if (c->s_dw) cudaStreamDestroy(c->s_dw);
+  if (c->s_comm) cudaStreamDestroy(c->s_comm);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return RT_OK;
@@ -1059,6 +1139,7 @@ RT_API int rt_update_weights(rt_ctx* c, uint32_t t, float lr, const rt_train_con
   cudaEventRecord(c->ev[6], c->stream);
   if ((rc = adam_impl(c, t, lr, tc, grad_scale, nullptr, 0.f, 0.f))) return rc;
   cudaEventRecord(c->ev[7], c->stream);
+  c->ev_recorded |= 8u;
   return wait_stream(c);
 }
 
@@ -1071,18 +1152,18 @@ static int train_step_device(rt_ctx* c, const rt::TokenBatch& tb, uint32_t step,
   c->cur = &tb;
   c->grads_zero_pending = true;  // grads.zero_out() (full_model.rs:675)
   if ((rc = forward_impl(c, batch, tc->softcap))) return rc;
-  if ((rc = backward_impl(c, tc->softcap, tc->loss_scale))) return rc;
-  cudaEventRecord(c->ev[4], c->stream);
-  if (c->world > 1 && c->dist_mode == RT_DIST_DATA_PARALLEL) {
-    if ((rc = rt_grad_allreduce(c))) return rc;
-  }
-  cudaEventRecord(c->ev[5], c->stream);
+  // data parallel: gradients are all-reduced bucket by bucket inside the backward
+  c->overlap_allreduce = c->world > 1 && c->dist_mode == RT_DIST_DATA_PARALLEL;
+  rc = backward_impl(c, tc->softcap, tc->loss_scale);
+  c->overlap_allreduce = false;
+  if (rc) return rc;
   cudaEventRecord(c->ev[6], c->stream);
   RT_OTHER(2, rt::sumsq_norm(c->grads, c->n_params, c->norm_partials, c->d_norm, c->stream), "grad norm");
   const float gsc = 1.0f / (static_cast<float>(batch) * static_cast<float>(c->world) * tc->loss_scale);
   const float lr = rt_learning_rate(step, tc);
   if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip))) return rc;
   cudaEventRecord(c->ev[7], c->stream);
+  c->ev_recorded |= 8u;
   if (!loss_out) return RT_OK;
   RT_CUDA(cudaMemcpyAsync(c->h_loss, c->d_loss, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss d2h");
   if ((rc = wait_stream(c))) return rc;
@@ -1227,12 +1308,15 @@ RT_API int rt_get_timings(rt_ctx* c, rt_timings* out) {
   if (!c || !out) return RT_ERR_ARG;
   cudaStreamSynchronize(c->stream);
   if (c->profiling) harvest_kernel_events(c);
-  float ms = 0.f;
   rt_timings t = c->acc;
-  if (cudaEventElapsedTime(&ms, c->ev[0], c->ev[1]) == cudaSuccess) t.fwd_ms = ms;
-  if (cudaEventElapsedTime(&ms, c->ev[2], c->ev[3]) == cudaSuccess) t.bwd_ms = ms;
-  if (cudaEventElapsedTime(&ms, c->ev[4], c->ev[5]) == cudaSuccess) t.comm_ms = ms;
-  if (cudaEventElapsedTime(&ms, c->ev[6], c->ev[7]) == cudaSuccess) t.opt_ms = ms;
+  double* dst[4] = {&t.fwd_ms, &t.bwd_ms, &t.comm_ms, &t.opt_ms};
+  for (int i = 0; i < 4; ++i) {
+    float ms = 0.f;
+    if ((c->ev_recorded >> i) & 1u) {
+      if (cudaEventElapsedTime(&ms, c->ev[2 * i], c->ev[2 * i + 1]) == cudaSuccess) *dst[i] = ms;
+      else cudaGetLastError();  // a pair still pending is not an error of the next launch
+    }
+  }
   *out = t;
   return RT_OK;
 }

@@ -96,11 +96,14 @@ struct rt_ctx {
   float* dy_b = nullptr;     // [M, D]
   float* dx_tmp = nullptr;   // [M, D]
   float* dx2 = nullptr;      // [M, D]
-  rt::bf16* dffn = nullptr;  // [M, D] alpha * dy
-  rt::bf16* dx2s = nullptr;  // [M, D] alpha * dx2
-  rt::bf16* da = nullptr;    // [M, D]
-  rt::bf16* dh13 = nullptr;  // [M, 2H]
-  rt::bf16* dqkv = nullptr;  // [M, 3D]
+  // Backward temporaries read by the weight-gradient GEMMs on the second
+  // stream: two copies each, by layer parity, so the data-gradient chain of
+  // layer l-1 can run while the weight gradients of layer l are computed.
+  rt::bf16* dffn[2] = {};  // [M, D] alpha * dy
+  rt::bf16* dx2s[2] = {};  // [M, D] alpha * dx2
+  rt::bf16* dh13[2] = {};  // [M, 2H]
+  rt::bf16* dqkv[2] = {};  // [M, 3D]
+  rt::bf16* da = nullptr;  // [M, D]
   float* dvec = nullptr;     // [B, heads, S]
   float* dgamma_part = nullptr;
 
@@ -132,8 +135,16 @@ struct rt_ctx {
   int world = 1, rank = 0, dist_mode = -1, timeout_ms = 0;
   rt::NcclState* nccl = nullptr;
 
+  // streams and events of the overlapped backward
+  cudaStream_t s_dw = nullptr;    // weight-gradient GEMMs
+  cudaStream_t s_comm = nullptr;  // data-parallel gradient all-reduce buckets
+  std::vector<cudaEvent_t> ev_dgate, ev_rms2, ev_attn, ev_dw_done, ev_comm;
+  cudaEvent_t ev_ce = nullptr, ev_de = nullptr, ev_main_done = nullptr, ev_comm_all = nullptr;
+  bool overlap_allreduce = false;  // set by the train step of a data-parallel context
+
   // timing
   cudaEvent_t ev[8] = {};
+  unsigned ev_recorded = 0;  // bit i: phase pair i (fwd, bwd, comm, opt) has been recorded
   bool profiling = false;
   std::vector<rt::KernelEvent> kevents;
   std::vector<cudaEvent_t> event_pool;

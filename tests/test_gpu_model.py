@@ -241,3 +241,16 @@ def test_backward_before_forward_is_state_error():
     k = CompiledKernels.compile(cfg, max_batch=1)
     with pytest.raises(RustaneError):
         k.backward(0.0, 1.0)
+
+
+def test_timings_query_leaves_no_cuda_error():
+    """rt_get_timings on a single-GPU context must not leave a CUDA error behind
+    (the all-reduce phase events are never recorded there)."""
+    cfg = SMALL
+    k = CompiledKernels.compile(cfg, max_batch=1)
+    k.upload_weights(ModelTensors.normal(cfg, seed=1))
+    tok, tgt = seeded(cfg, 1)
+    k.train_step(tok, tgt, 0, TrainConfig())
+    t = k.timings()
+    assert t["fwd_ms"] > 0 and t["bwd_ms"] > 0 and t["comm_ms"] == 0
+    k.train_step(tok, tgt, 1, TrainConfig())  # the next launch must still succeed
