@@ -416,6 +416,62 @@ __global__ void init_normal_kernel(float* __restrict__ dst, int64_t n, uint64_t 
     if (2 * i + 1 < n) dst[2 * i + 1] = r * sn;
   }
 }
+// x_out = x + alpha * p; optional RMSNorm of x_out (one warp per row)
+__global__ void residual_rmsnorm_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ p, float alpha,
+                                        const float* __restrict__ gamma, float* __restrict__ x_out,
+                                        __nv_bfloat16* __restrict__ xn, float* __restrict__ rms_inv, int M, int D) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int64_t off = static_cast<int64_t>(row) * D;
+  const float4* xr = reinterpret_cast<const float4*>(x + off);
+  const uint2* pr = reinterpret_cast<const uint2*>(p + off);
+  float4* outr = reinterpret_cast<float4*>(x_out + off);
+  const int D4 = D >> 2;
+  float ss = 0.f;
+  for (int c = lane; c < D4; c += 32) {
+    const float4 a = xr[c];
+    const uint2 q = pr[c];
+    float4 v;
+    v.x = a.x + alpha * bf16lo(q.x);
+    v.y = a.y + alpha * bf16hi(q.x);
+    v.z = a.z + alpha * bf16lo(q.y);
+    v.w = a.w + alpha * bf16hi(q.y);
+    outr[c] = v;
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  if (!gamma) return;
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(D)) + kRmsEps);
+  if (lane == 0) rms_inv[row] = r;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  uint2* o = reinterpret_cast<uint2*>(xn + off);
+  for (int c = lane; c < D4; c += 32) {
+    const float4 v = outr[c], g = g4[c];
+    o[c] = make_uint2(pack_bf16x2(v.x * r * g.x, v.y * r * g.y), pack_bf16x2(v.z * r * g.z, v.w * r * g.w));
+  }
+}
+
+__device__ __forceinline__ float normal_at(uint64_t seed, int64_t g, float std) {
+  const uint64_t h = splitmix64(seed ^ splitmix64(static_cast<uint64_t>(g >> 1)));
+  const float u1 = (static_cast<float>(h >> 40) + 1.0f) * (1.0f / 16777217.0f);
+  const float u2 = static_cast<float>((h >> 16) & 0xFFFFFFull) * (1.0f / 16777216.0f);
+  const float r = sqrtf(-2.0f * logf(u1)) * std;
+  float sn, cs;
+  sincospif(2.0f * u2, &sn, &cs);
+  return (g & 1) ? r * sn : r * cs;
+}
+
+__global__ void init_normal_block_kernel(float* __restrict__ dst, int64_t rows, int64_t cols, int64_t dst_ld,
+                                         int64_t gbase, int64_t gld, int64_t gcol0, uint64_t seed, float std) {
+  const int64_t n = rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    dst[r * dst_ld + c] = normal_at(seed, gbase + r * gld + gcol0 + c, std);
+  }
+}
+
 __global__ void nonfinite_kernel(const float* __restrict__ x, int64_t n, int* flag) {
   bool bad = false;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -522,6 +578,18 @@ int init_normal(float* dst, int64_t n, uint64_t seed, float std, cudaStream_t s)
 }
 int scale_f32(const float* x, float* y, int64_t n, float a, cudaStream_t s) {
   scale_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n, a);
+  return cudaGetLastError();
+}
+int residual_rmsnorm_fwd(const float* x, const __nv_bfloat16* p, float alpha, const float* gamma, float* x_out,
+                         __nv_bfloat16* xn, float* rms_inv, int M, int D, cudaStream_t s) {
+  if (D % 4) return -1;
+  residual_rmsnorm_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, p, alpha, gamma, x_out, xn, rms_inv, M, D);
+  return cudaGetLastError();
+}
+int init_normal_block(float* dst, int64_t rows, int64_t cols, int64_t dst_ld, int64_t gbase, int64_t gld,
+                      int64_t gcol0, uint64_t seed, float std, cudaStream_t s) {
+  init_normal_block_kernel<<<grid_for(rows * cols, 256), 256, 0, s>>>(dst, rows, cols, dst_ld, gbase, gld, gcol0,
+                                                                      seed, std);
   return cudaGetLastError();
 }
 int nonfinite_check(const float* x, int64_t n, int* flag, cudaStream_t s) {

@@ -67,6 +67,16 @@ struct AdamArgs {
 };
 int adam_step(const AdamArgs& a, cudaStream_t s);
 
+// Tensor-parallel residual: x_out = x + alpha * p (p = all-reduced bf16 partial
+// of a row-parallel GEMM); with gamma, also xn = RMSNorm(x_out) and rms_inv.
+int residual_rmsnorm_fwd(const float* x, const __nv_bfloat16* p, float alpha, const float* gamma, float* x_out,
+                         __nv_bfloat16* xn, float* rms_inv, int M, int D, cudaStream_t s);
+// Fill a [rows, cols] block (row stride dst_ld) with the N(0, std) stream of
+// init_normal at global element indices gbase + r * gld + gcol0 + c, so a shard
+// gets exactly the values of the same block of the full parameter arena.
+int init_normal_block(float* dst, int64_t rows, int64_t cols, int64_t dst_ld, int64_t gbase, int64_t gld,
+                      int64_t gcol0, uint64_t seed, float std, cudaStream_t s);
+
 // Elementwise helpers.
 int cast_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s);
 int fill_f32(float* dst, int64_t n, float value, cudaStream_t s);

@@ -105,9 +105,20 @@ T* dalloc(rt_ctx* c, int64_t count) {
   size_t bytes = (static_cast<size_t>(count) * sizeof(T) + 255) & ~size_t(255);
   void* p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
-  c->allocations.push_back(p);
+  c->allocations.push_back({p, bytes});
   c->device_bytes += static_cast<int64_t>(bytes);
   return static_cast<T*>(p);
+}
+
+void dfree(rt_ctx* c, void* p) {
+  if (!p) return;
+  for (size_t i = 0; i < c->allocations.size(); ++i)
+    if (c->allocations[i].first == p) {
+      c->device_bytes -= static_cast<int64_t>(c->allocations[i].second);
+      c->allocations.erase(c->allocations.begin() + static_cast<long>(i));
+      cudaFree(p);
+      return;
+    }
 }
 
 cudaEvent_t pool_event(rt_ctx* c) {
@@ -257,16 +268,21 @@ void compute_rope_tables(const rt_model_config& cfg, std::vector<float>& cf, std
 
 // ------------------------------------------------------------ host copies
 // Copy a [rows, cols] host matrix into columns [col0, col0+cols) of a device
-// matrix with row stride ld (elements), or back.
-int copy_block_h2d(rt_ctx* c, float* dst, int64_t ld, int64_t col0, const float* src, int64_t rows, int64_t cols) {
-  RT_CUDA(cudaMemcpy2D(dst + col0, ld * sizeof(float), src, cols * sizeof(float), cols * sizeof(float), rows,
-                       cudaMemcpyHostToDevice),
+// matrix with row stride ld (elements), or back.  Every host <-> device copy of
+// the context is ordered on its own (non-blocking) stream: a plain cudaMemcpy
+// from pageable memory may return before its DMA lands and is not ordered with
+// kernels on a non-blocking stream.
+int copy_block_h2d(rt_ctx* c, float* dst, int64_t ld, int64_t col0, const float* src, int64_t rows, int64_t cols,
+                   int64_t src_ld = 0) {
+  if (src_ld == 0) src_ld = cols;
+  RT_CUDA(cudaMemcpy2DAsync(dst + col0, ld * sizeof(float), src, src_ld * sizeof(float), cols * sizeof(float), rows,
+                       cudaMemcpyHostToDevice, c->stream),
           "upload");
   return RT_OK;
 }
 int copy_block_d2h(rt_ctx* c, float* dst, const float* src, int64_t ld, int64_t col0, int64_t rows, int64_t cols) {
-  RT_CUDA(cudaMemcpy2D(dst, cols * sizeof(float), src + col0, ld * sizeof(float), cols * sizeof(float), rows,
-                       cudaMemcpyDeviceToHost),
+  RT_CUDA(cudaMemcpy2DAsync(dst, cols * sizeof(float), src + col0, ld * sizeof(float), cols * sizeof(float), rows,
+                       cudaMemcpyDeviceToHost, c->stream),
           "download");
   return RT_OK;
 }
@@ -276,9 +292,9 @@ int arena_h2d(rt_ctx* c, float* arena, const rt_model_ptrs* h) {
   const auto& cfg = c->cfg;
   const int64_t D = cfg.dim, H = cfg.hidden, Q = cfg.q_dim;
   if (!h || !h->embed || !h->gamma_final || !h->layers) return set_err(c, RT_ERR_ARG, "null model pointers");
-  RT_CUDA(cudaMemcpy(arena, h->embed, sizeof(float) * cfg.vocab * D, cudaMemcpyHostToDevice), "upload embed");
+  RT_CUDA(cudaMemcpyAsync(arena, h->embed, sizeof(float) * cfg.vocab * D, cudaMemcpyHostToDevice, c->stream), "upload embed");
   float* gb = arena + c->n_matrix_end;
-  RT_CUDA(cudaMemcpy(gb, h->gamma_final, sizeof(float) * D, cudaMemcpyHostToDevice), "upload gamma_final");
+  RT_CUDA(cudaMemcpyAsync(gb, h->gamma_final, sizeof(float) * D, cudaMemcpyHostToDevice, c->stream), "upload gamma_final");
   for (int l = 0; l < cfg.nlayers; ++l) {
     const rt_layer_ptrs& L = h->layers[l];
     const auto& o = c->layer_off[l];
@@ -288,12 +304,12 @@ int arena_h2d(rt_ctx* c, float* arena, const rt_model_ptrs* h) {
     if ((rc = copy_block_h2d(c, arena + o.wqkv, 3 * D, 0, L.wq, D, D))) return rc;
     if ((rc = copy_block_h2d(c, arena + o.wqkv, 3 * D, D, L.wk, D, D))) return rc;
     if ((rc = copy_block_h2d(c, arena + o.wqkv, 3 * D, 2 * D, L.wv, D, D))) return rc;
-    RT_CUDA(cudaMemcpy(arena + o.wo, L.wo, sizeof(float) * Q * D, cudaMemcpyHostToDevice), "upload wo");
+    RT_CUDA(cudaMemcpyAsync(arena + o.wo, L.wo, sizeof(float) * Q * D, cudaMemcpyHostToDevice, c->stream), "upload wo");
     if ((rc = copy_block_h2d(c, arena + o.w13, 2 * H, 0, L.w1, D, H))) return rc;
     if ((rc = copy_block_h2d(c, arena + o.w13, 2 * H, H, L.w3, D, H))) return rc;
-    RT_CUDA(cudaMemcpy(arena + o.w2, L.w2, sizeof(float) * D * H, cudaMemcpyHostToDevice), "upload w2");
-    RT_CUDA(cudaMemcpy(arena + o.gamma1, L.gamma1, sizeof(float) * D, cudaMemcpyHostToDevice), "upload gamma1");
-    RT_CUDA(cudaMemcpy(arena + o.gamma2, L.gamma2, sizeof(float) * D, cudaMemcpyHostToDevice), "upload gamma2");
+    RT_CUDA(cudaMemcpyAsync(arena + o.w2, L.w2, sizeof(float) * D * H, cudaMemcpyHostToDevice, c->stream), "upload w2");
+    RT_CUDA(cudaMemcpyAsync(arena + o.gamma1, L.gamma1, sizeof(float) * D, cudaMemcpyHostToDevice, c->stream), "upload gamma1");
+    RT_CUDA(cudaMemcpyAsync(arena + o.gamma2, L.gamma2, sizeof(float) * D, cudaMemcpyHostToDevice, c->stream), "upload gamma2");
   }
   return RT_OK;
 }
@@ -302,8 +318,8 @@ int arena_d2h(rt_ctx* c, const float* arena, const rt_model_ptrs* h) {
   const auto& cfg = c->cfg;
   const int64_t D = cfg.dim, H = cfg.hidden, Q = cfg.q_dim;
   if (!h || !h->embed || !h->gamma_final || !h->layers) return set_err(c, RT_ERR_ARG, "null model pointers");
-  RT_CUDA(cudaMemcpy(h->embed, arena, sizeof(float) * cfg.vocab * D, cudaMemcpyDeviceToHost), "download embed");
-  RT_CUDA(cudaMemcpy(h->gamma_final, arena + c->n_matrix_end, sizeof(float) * D, cudaMemcpyDeviceToHost),
+  RT_CUDA(cudaMemcpyAsync(h->embed, arena, sizeof(float) * cfg.vocab * D, cudaMemcpyDeviceToHost, c->stream), "download embed");
+  RT_CUDA(cudaMemcpyAsync(h->gamma_final, arena + c->n_matrix_end, sizeof(float) * D, cudaMemcpyDeviceToHost, c->stream),
           "download gamma_final");
   for (int l = 0; l < cfg.nlayers; ++l) {
     const rt_layer_ptrs& L = h->layers[l];
@@ -312,12 +328,12 @@ int arena_d2h(rt_ctx* c, const float* arena, const rt_model_ptrs* h) {
     if ((rc = copy_block_d2h(c, L.wq, arena + o.wqkv, 3 * D, 0, D, D))) return rc;
     if ((rc = copy_block_d2h(c, L.wk, arena + o.wqkv, 3 * D, D, D, D))) return rc;
     if ((rc = copy_block_d2h(c, L.wv, arena + o.wqkv, 3 * D, 2 * D, D, D))) return rc;
-    RT_CUDA(cudaMemcpy(L.wo, arena + o.wo, sizeof(float) * Q * D, cudaMemcpyDeviceToHost), "download wo");
+    RT_CUDA(cudaMemcpyAsync(L.wo, arena + o.wo, sizeof(float) * Q * D, cudaMemcpyDeviceToHost, c->stream), "download wo");
     if ((rc = copy_block_d2h(c, L.w1, arena + o.w13, 2 * H, 0, D, H))) return rc;
     if ((rc = copy_block_d2h(c, L.w3, arena + o.w13, 2 * H, H, D, H))) return rc;
-    RT_CUDA(cudaMemcpy(L.w2, arena + o.w2, sizeof(float) * D * H, cudaMemcpyDeviceToHost), "download w2");
-    RT_CUDA(cudaMemcpy(L.gamma1, arena + o.gamma1, sizeof(float) * D, cudaMemcpyDeviceToHost), "download gamma1");
-    RT_CUDA(cudaMemcpy(L.gamma2, arena + o.gamma2, sizeof(float) * D, cudaMemcpyDeviceToHost), "download gamma2");
+    RT_CUDA(cudaMemcpyAsync(L.w2, arena + o.w2, sizeof(float) * D * H, cudaMemcpyDeviceToHost, c->stream), "download w2");
+    RT_CUDA(cudaMemcpyAsync(L.gamma1, arena + o.gamma1, sizeof(float) * D, cudaMemcpyDeviceToHost, c->stream), "download gamma1");
+    RT_CUDA(cudaMemcpyAsync(L.gamma2, arena + o.gamma2, sizeof(float) * D, cudaMemcpyDeviceToHost, c->stream), "download gamma2");
   }
   return RT_OK;
 }
@@ -384,57 +400,144 @@ int upload_tokens(rt_ctx* c, rt::TokenBatch& tb, const uint32_t* tokens, const u
   return RT_OK;
 }
 
+// bf16 weight arena: [embed | per layer Wqkv D x 3Dl, Wo Dl x D, W13 D x 2Hl, W2 D x Hl] with
+// Dl = this rank's heads * hd and Hl its hidden columns (the full sizes without TP).
+void layout_bf16(rt_ctx* c) {
+  const int64_t D = c->cfg.dim, Dl = int64_t(c->heads_loc) * c->cfg.hd, Hl = c->hid_loc;
+  c->layer_off_b.resize(c->cfg.nlayers);
+  int64_t off = int64_t(c->cfg.vocab) * D;
+  for (auto& o : c->layer_off_b) {
+    o.wqkv = off;
+    off += D * 3 * Dl;
+    o.wo = off;
+    off += Dl * D;
+    o.w13 = off;
+    off += D * 2 * Hl;
+    o.w2 = off;
+    off += D * Hl;
+    o.gamma1 = o.gamma2 = 0;
+  }
+  c->n_bf16 = off;
+}
+
+// Buffers whose size depends on the shard: bf16 weights, q/k/v, attention
+// output, lse, h1|h3, gate, and the TP partial.  Returns false on OOM.
+bool alloc_shard_buffers(rt_ctx* c) {
+  const int64_t M = int64_t(c->max_batch) * c->cfg.seq, Dl = int64_t(c->heads_loc) * c->cfg.hd, Hl = c->hid_loc;
+  bool ok = true;
+  auto need = [&](void* p) { ok = ok && p != nullptr; };
+  c->params_bf16 = dalloc<bf16>(c, c->n_bf16);
+  need(c->params_bf16);
+  for (auto& A : c->acts) {
+    A.qkv = dalloc<bf16>(c, M * 3 * Dl);
+    A.attn = dalloc<bf16>(c, M * Dl);
+    A.lse2 = dalloc<float>(c, M * c->heads_loc);
+    A.h13 = dalloc<bf16>(c, M * 2 * Hl);
+    A.gate = dalloc<bf16>(c, M * Hl);
+    for (void* p : {(void*)A.qkv, (void*)A.attn, (void*)A.lse2, (void*)A.h13, (void*)A.gate}) need(p);
+  }
+  if (c->tp) {
+    c->tp_partial = dalloc<bf16>(c, M * c->cfg.dim);
+    need(c->tp_partial);
+  }
+  return ok;
+}
+
+void free_shard_buffers(rt_ctx* c) {
+  dfree(c, c->params_bf16);
+  c->params_bf16 = nullptr;
+  for (auto& A : c->acts) {
+    for (void* p : {(void*)A.qkv, (void*)A.attn, (void*)A.lse2, (void*)A.h13, (void*)A.gate}) dfree(c, p);
+    A.qkv = A.attn = A.h13 = A.gate = nullptr;
+    A.lse2 = nullptr;
+  }
+  dfree(c, c->tp_partial);
+  c->tp_partial = nullptr;
+}
+
+// Sum of the row-parallel GEMM partials over the tensor-parallel ranks (bf16).
+int tp_allreduce(rt_ctx* c, int64_t n) {
+  rt::NcclApi* api = rt::nccl_api();
+  if (!api || !c->nccl || !c->nccl->comm) return set_err(c, RT_ERR_NCCL, "no communicator (aborted or not initialised)");
+  ncclResult_t r = api->allReduce(c->tp_partial, c->tp_partial, static_cast<size_t>(n), ncclBfloat16, ncclSum,
+                                  c->nccl->comm, c->stream);
+  if (r != ncclSuccess) return set_err(c, RT_ERR_NCCL, std::string("ncclAllReduce: ") + api->errorString(r));
+  return RT_OK;
+}
+
 // ---------------------------------------------------------------- forward
 int layer_forward(rt_ctx* c, int l, const rt::LayerActs& A, const float* x_in, float* x_next, int batch) {
   const auto& cfg = c->cfg;
-  const int D = cfg.dim, H = cfg.hidden, S = cfg.seq, M = batch * S;
+  const int D = cfg.dim, S = cfg.seq, M = batch * S;
+  const int Dl = c->heads_loc * cfg.hd, Hl = c->hid_loc;  // this rank's shard (everything without TP)
   const float alpha = alpha_of(cfg);
   const auto& o = c->layer_off[l];
+  const auto& ob = c->layer_off_b[l];
   const bf16* W = c->params_bf16;
   const float* G = gamma_base(c);
   const int64_t goff = c->n_matrix_end;  // gamma offsets are relative to gamma_base()
   int rc;
   RT_OTHER(1, rt::rmsnorm_fwd(x_in, G + (o.gamma1 - goff), A.xn, A.rms1, M, D, c->stream), "rmsnorm1");
-  {  // Q K V projection + RoPE (sdpaFwd, kernels/sdpa_fwd.rs:80-128)
+  {  // Q K V projection + RoPE (sdpaFwd, kernels/sdpa_fwd.rs:80-128); TP: this rank's heads
     rt::GemmArgs g;
     g.a = A.xn; g.lda = D;
-    g.b = W + o.wqkv; g.ldb = 3 * D; g.b_mn = true;
-    g.M = M; g.N = 3 * D; g.K = D;
-    g.epi = rt::kEpiRope; g.out = A.qkv; g.ldo = 3 * D;
-    g.rope_cos = c->rope_cos_f; g.rope_sin = c->rope_sin_f; g.seq = S; g.rope_cols = 2 * D;
+    g.b = W + ob.wqkv; g.ldb = 3 * Dl; g.b_mn = true;
+    g.M = M; g.N = 3 * Dl; g.K = D;
+    g.epi = rt::kEpiRope; g.out = A.qkv; g.ldo = 3 * Dl;
+    g.rope_cos = c->rope_cos_f; g.rope_sin = c->rope_sin_f; g.seq = S; g.rope_cols = 2 * Dl;
     if ((rc = gemm(c, g, "qkv"))) return rc;
   }
   {  // causal attention (sdpa_fwd.rs:130-150)
     rt::AttnArgs a;
-    a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
-    a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
-    const double fl = 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
+    a.batch = batch; a.S = S; a.heads = c->heads_loc; a.hd = cfg.hd; a.D = Dl;
+    a.qkv = A.qkv; a.ldq = 3 * Dl; a.out = A.attn; a.ldo = Dl; a.lse2 = A.lse2;
+    const double fl = 4.0 * batch * c->heads_loc * double(S) * S / 2.0 * cfg.hd;
     RT_LAUNCH(launch(c, 1, fl, 1, [&] { return rt::attn_forward(a, c->stream); }), "attention fwd");
   }
-  {  // woFwd + residual x2 = x + alpha * o (layer.rs:769-784)
+  if (!c->tp) {  // woFwd + residual x2 = x + alpha * o (layer.rs:769-784)
     rt::GemmArgs g;
-    g.a = A.attn; g.lda = D;
-    g.b = W + o.wo; g.ldb = D; g.b_mn = true;
-    g.M = M; g.N = D; g.K = cfg.q_dim;
+    g.a = A.attn; g.lda = Dl;
+    g.b = W + ob.wo; g.ldb = D; g.b_mn = true;
+    g.M = M; g.N = D; g.K = Dl;
     g.epi = rt::kEpiResidual; g.aux = x_in; g.ld_aux = D; g.out = A.x2; g.ldo = D; g.alpha = alpha;
     if ((rc = gemm(c, g, "wo"))) return rc;
+    RT_OTHER(1, rt::rmsnorm_fwd(A.x2, G + (o.gamma2 - goff), A.x2n, A.rms2, M, D, c->stream), "rmsnorm2");
+  } else {  // row-parallel Wo: partial -> all-reduce -> x2 = x + alpha * sum, RMSNorm2
+    rt::GemmArgs g;
+    g.a = A.attn; g.lda = Dl;
+    g.b = W + ob.wo; g.ldb = D; g.b_mn = true;
+    g.M = M; g.N = D; g.K = Dl;
+    g.epi = rt::kEpiBf16; g.out = c->tp_partial; g.ldo = D;
+    if ((rc = gemm(c, g, "wo (row-parallel)"))) return rc;
+    if ((rc = tp_allreduce(c, int64_t(M) * D))) return rc;
+    RT_OTHER(1, rt::residual_rmsnorm_fwd(x_in, c->tp_partial, alpha, G + (o.gamma2 - goff), A.x2, A.x2n, A.rms2, M,
+                                         D, c->stream),
+             "residual + rmsnorm2");
   }
-  RT_OTHER(1, rt::rmsnorm_fwd(A.x2, G + (o.gamma2 - goff), A.x2n, A.rms2, M, D, c->stream), "rmsnorm2");
-  {  // W1 | W3 + SwiGLU (ffn_fused.rs:46-63)
+  {  // W1 | W3 + SwiGLU (ffn_fused.rs:46-63); TP: this rank's hidden columns
     rt::GemmArgs g;
     g.a = A.x2n; g.lda = D;
-    g.b = W + o.w13; g.ldb = 2 * H; g.b_mn = true;
-    g.M = M; g.N = H; g.K = D;
-    g.epi = rt::kEpiSwiglu; g.out = A.h13; g.ldo = 2 * H; g.out2 = A.gate; g.ldo2 = H; g.n_half = H;
+    g.b = W + ob.w13; g.ldb = 2 * Hl; g.b_mn = true;
+    g.M = M; g.N = Hl; g.K = D;
+    g.epi = rt::kEpiSwiglu; g.out = A.h13; g.ldo = 2 * Hl; g.out2 = A.gate; g.ldo2 = Hl; g.n_half = Hl;
     if ((rc = gemm(c, g, "w13"))) return rc;
   }
-  {  // gate W2^T + residual (ffn_fused.rs:65-78)
+  {  // gate W2^T + residual (ffn_fused.rs:65-78); TP: row-parallel + all-reduce
     rt::GemmArgs g;
-    g.a = A.gate; g.lda = H;
-    g.b = W + o.w2; g.ldb = H; g.b_mn = false;
-    g.M = M; g.N = D; g.K = H;
-    g.epi = rt::kEpiResidual; g.aux = A.x2; g.ld_aux = D; g.out = x_next; g.ldo = D; g.alpha = alpha;
-    if ((rc = gemm(c, g, "w2"))) return rc;
+    g.a = A.gate; g.lda = Hl;
+    g.b = W + ob.w2; g.ldb = Hl; g.b_mn = false;
+    g.M = M; g.N = D; g.K = Hl;
+    if (!c->tp) {
+      g.epi = rt::kEpiResidual; g.aux = A.x2; g.ld_aux = D; g.out = x_next; g.ldo = D; g.alpha = alpha;
+      if ((rc = gemm(c, g, "w2"))) return rc;
+    } else {
+      g.epi = rt::kEpiBf16; g.out = c->tp_partial; g.ldo = D;
+      if ((rc = gemm(c, g, "w2 (row-parallel)"))) return rc;
+      if ((rc = tp_allreduce(c, int64_t(M) * D))) return rc;
+      RT_OTHER(1, rt::residual_rmsnorm_fwd(A.x2, c->tp_partial, alpha, nullptr, x_next, nullptr, nullptr, M, D,
+                                           c->stream),
+               "residual");
+    }
   }
   return RT_OK;
 }
@@ -808,26 +911,23 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
     need(c->mom1);
     need(c->mom2);
   }
-  c->params_bf16 = dalloc<bf16>(c, c->n_matrix_end);
-  need(c->params_bf16);
+  c->heads_loc = cfg.heads;
+  c->head0 = 0;
+  c->hid_loc = cfg.hidden;
+  c->hid0 = 0;
+  layout_bf16(c);
   const int nact = fo ? 1 : static_cast<int>(L);
   c->acts.resize(nact);
   for (auto& A : c->acts) {
     A.x = dalloc<float>(c, M * D);
     A.xn = dalloc<bf16>(c, M * D);
     A.rms1 = dalloc<float>(c, M);
-    A.qkv = dalloc<bf16>(c, M * 3 * D);
-    A.attn = dalloc<bf16>(c, M * D);
-    A.lse2 = dalloc<float>(c, M * cfg.heads);
     A.x2 = dalloc<float>(c, M * D);
     A.x2n = dalloc<bf16>(c, M * D);
     A.rms2 = dalloc<float>(c, M);
-    A.h13 = dalloc<bf16>(c, M * 2 * H);
-    A.gate = dalloc<bf16>(c, M * H);
-    for (void* p : {(void*)A.x, (void*)A.xn, (void*)A.rms1, (void*)A.qkv, (void*)A.attn, (void*)A.lse2, (void*)A.x2,
-                    (void*)A.x2n, (void*)A.rms2, (void*)A.h13, (void*)A.gate})
-      need(p);
+    for (void* p : {(void*)A.x, (void*)A.xn, (void*)A.rms1, (void*)A.x2, (void*)A.x2n, (void*)A.rms2}) need(p);
   }
+  if (!alloc_shard_buffers(c)) ok = false;
   c->x_out = dalloc<float>(c, M * D);
   c->xf = dalloc<bf16>(c, M * D);
   c->rms_f = dalloc<float>(c, M);
@@ -900,7 +1000,7 @@ RT_API int rt_ctx_destroy(rt_ctx* c) {
     }
     delete c->nccl;
   }
-  for (void* p : c->allocations) cudaFree(p);
+  for (auto& a : c->allocations) cudaFree(a.first);
   if (c->h_stage) cudaFreeHost(c->h_stage);
   if (c->h_loss) cudaFreeHost(c->h_loss);
   for (auto& e : c->ev)
@@ -933,41 +1033,51 @@ RT_API int rt_weights_upload(rt_ctx* c, const rt_model_ptrs* w) {
   if (!forward_only(c)) {
     if ((rc = arena_h2d(c, c->params, w))) return rc;
     RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_matrix_end, c->stream), "cast bf16");
+    c->weights_set = true;
   } else {
-    // compact fp32 [embed | gammas]; matrices go through a bounded fp32 staging buffer
-    RT_CUDA(cudaMemcpy(c->params, w->embed, sizeof(float) * c->n_embed, cudaMemcpyHostToDevice), "upload embed");
+    // compact fp32 [embed | gammas]; this rank's matrix shard goes through a bounded fp32 staging buffer
+    RT_CUDA(cudaMemcpyAsync(c->params, w->embed, sizeof(float) * c->n_embed, cudaMemcpyHostToDevice, c->stream), "upload embed");
     RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_embed, c->stream), "cast bf16");
     float* gb = gamma_base(c);
-    RT_CUDA(cudaMemcpy(gb, w->gamma_final, sizeof(float) * D, cudaMemcpyHostToDevice), "gamma_final");
-    const int64_t biggest = std::max<int64_t>(D * 3 * D, D * 2 * cfg.hidden);
+    RT_CUDA(cudaMemcpyAsync(gb, w->gamma_final, sizeof(float) * D, cudaMemcpyHostToDevice, c->stream), "gamma_final");
+    const int64_t H = cfg.hidden, Dl = int64_t(c->heads_loc) * cfg.hd, Hl = c->hid_loc;
+    const int64_t q0 = int64_t(c->head0) * cfg.hd, h0 = c->hid0;
+    const int64_t biggest = std::max<int64_t>(std::max<int64_t>(D * 3 * Dl, D * 2 * Hl), Dl * D);
     float* stage = nullptr;
     RT_CUDA(cudaMalloc(&stage, sizeof(float) * biggest), "staging");
     rc = 0;
     for (int l = 0; l < cfg.nlayers && rc == 0; ++l) {
       const auto& o = c->layer_off[l];
+      const auto& ob = c->layer_off_b[l];
       const rt_layer_ptrs& L = w->layers[l];
-      const int64_t H = cfg.hidden;
-      rc = 0;
-      if (!rc) rc = copy_block_h2d(c, stage, 3 * D, 0, L.wq, D, D);
-      if (!rc) rc = copy_block_h2d(c, stage, 3 * D, D, L.wk, D, D);
-      if (!rc) rc = copy_block_h2d(c, stage, 3 * D, 2 * D, L.wv, D, D);
-      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.wqkv, D * 3 * D, c->stream) ? RT_ERR_CUDA : 0;
-      if (!rc) rc = cudaMemcpy(stage, L.wo, sizeof(float) * D * D, cudaMemcpyHostToDevice) ? RT_ERR_CUDA : 0;
-      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.wo, D * D, c->stream) ? RT_ERR_CUDA : 0;
-      if (!rc) rc = copy_block_h2d(c, stage, 2 * H, 0, L.w1, D, H);
-      if (!rc) rc = copy_block_h2d(c, stage, 2 * H, H, L.w3, D, H);
-      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.w13, D * 2 * H, c->stream) ? RT_ERR_CUDA : 0;
-      if (!rc) rc = cudaMemcpy(stage, L.w2, sizeof(float) * D * H, cudaMemcpyHostToDevice) ? RT_ERR_CUDA : 0;
-      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + o.w2, D * H, c->stream) ? RT_ERR_CUDA : 0;
-      if (!rc) rc = cudaMemcpy(gb + (o.gamma1 - c->n_matrix_end), L.gamma1, sizeof(float) * D, cudaMemcpyHostToDevice)
+      // Wq | Wk | Wv columns of this rank's heads
+      if (!rc) rc = copy_block_h2d(c, stage, 3 * Dl, 0, L.wq + q0, D, Dl, D);
+      if (!rc) rc = copy_block_h2d(c, stage, 3 * Dl, Dl, L.wk + q0, D, Dl, D);
+      if (!rc) rc = copy_block_h2d(c, stage, 3 * Dl, 2 * Dl, L.wv + q0, D, Dl, D);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.wqkv, D * 3 * Dl, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaStreamSynchronize(c->stream) ? RT_ERR_CUDA : 0;
+      // Wo rows of this rank's heads
+      if (!rc) rc = cudaMemcpyAsync(stage, L.wo + q0 * D, sizeof(float) * Dl * D, cudaMemcpyHostToDevice, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.wo, Dl * D, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaStreamSynchronize(c->stream) ? RT_ERR_CUDA : 0;
+      // W1 | W3 columns of this rank's hidden units
+      if (!rc) rc = copy_block_h2d(c, stage, 2 * Hl, 0, L.w1 + h0, D, Hl, H);
+      if (!rc) rc = copy_block_h2d(c, stage, 2 * Hl, Hl, L.w3 + h0, D, Hl, H);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.w13, D * 2 * Hl, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaStreamSynchronize(c->stream) ? RT_ERR_CUDA : 0;
+      // W2 columns of this rank's hidden units
+      if (!rc) rc = copy_block_h2d(c, stage, Hl, 0, L.w2 + h0, D, Hl, H);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.w2, D * Hl, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaStreamSynchronize(c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaMemcpyAsync(gb + (o.gamma1 - c->n_matrix_end), L.gamma1, sizeof(float) * D, cudaMemcpyHostToDevice, c->stream)
                         ? RT_ERR_CUDA : 0;
-      if (!rc) rc = cudaMemcpy(gb + (o.gamma2 - c->n_matrix_end), L.gamma2, sizeof(float) * D, cudaMemcpyHostToDevice)
+      if (!rc) rc = cudaMemcpyAsync(gb + (o.gamma2 - c->n_matrix_end), L.gamma2, sizeof(float) * D, cudaMemcpyHostToDevice, c->stream)
                         ? RT_ERR_CUDA : 0;
-      cudaStreamSynchronize(c->stream);
     }
     cudaFree(stage);
     if (rc) return set_err(c, rc, "forward-only upload failed");
   }
+  c->weights_set = true;
   RT_CUDA(cudaStreamSynchronize(c->stream), "upload sync");
   return RT_OK;
 }
@@ -1030,26 +1140,42 @@ RT_API int rt_weights_init_normal(rt_ctx* c, uint64_t seed, float std) {
     RT_CUDA(cudaMemsetAsync(c->mom2, 0, sizeof(float) * c->n_params, c->stream), "zero v");
     c->grads_zero_pending = true;
   } else {
-    // embed straight into the compact fp32 buffer, matrices through a bounded staging buffer
+    // embed straight into the compact fp32 buffer; each matrix shard is generated at
+    // the global indices of the full arena (same values as a training context / any TP degree)
     RT_LAUNCH(rt::init_normal(c->params, c->n_embed, seed, std, c->stream), "init embed");
     RT_LAUNCH(rt::fill_f32(gamma_base(c), n_gam, 1.0f, c->stream), "init gammas");
     RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_embed, c->stream), "cast embed");
-    const int64_t chunk = int64_t(64) << 20;  // elements
+    const auto& cfg = c->cfg;
+    const int64_t H = cfg.hidden, Dl = int64_t(c->heads_loc) * cfg.hd, Hl = c->hid_loc;
+    const int64_t q0 = int64_t(c->head0) * cfg.hd, h0 = c->hid0;
+    const int64_t biggest = std::max<int64_t>(std::max<int64_t>(D * 3 * Dl, D * 2 * Hl), Dl * D);
     float* stage = nullptr;
-    RT_CUDA(cudaMalloc(&stage, sizeof(float) * chunk), "staging");
-    for (int64_t b = c->n_embed; b < c->n_matrix_end; b += chunk) {
-      const int64_t n = std::min(chunk, c->n_matrix_end - b);
-      // the same counter stream as a training context: element i of the arena
-      int rc1 = rt::init_normal(stage, n, seed ^ (0x9E3779B97F4A7C15ull * uint64_t(b / chunk + 1)), std, c->stream);
-      int rc2 = rt::cast_bf16(stage, c->params_bf16 + b, n, c->stream);
-      if (rc1 || rc2) {
-        cudaFree(stage);
-        return set_err(c, RT_ERR_CUDA, "init normal (forward-only)");
-      }
+    RT_CUDA(cudaMalloc(&stage, sizeof(float) * biggest), "staging");
+    int rc = 0;
+    auto blk = [&](float* dst, int64_t rows, int64_t cols, int64_t dst_ld, int64_t gbase, int64_t gld, int64_t gcol0) {
+      if (rc) return;
+      rc = rt::init_normal_block(dst, rows, cols, dst_ld, gbase, gld, gcol0, seed, std, c->stream) ? RT_ERR_CUDA : 0;
+    };
+    for (int l = 0; l < cfg.nlayers && rc == 0; ++l) {
+      const auto& o = c->layer_off[l];
+      const auto& ob = c->layer_off_b[l];
+      blk(stage, D, Dl, 3 * Dl, o.wqkv, 3 * D, q0);
+      blk(stage + Dl, D, Dl, 3 * Dl, o.wqkv, 3 * D, D + q0);
+      blk(stage + 2 * Dl, D, Dl, 3 * Dl, o.wqkv, 3 * D, 2 * D + q0);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.wqkv, D * 3 * Dl, c->stream) ? RT_ERR_CUDA : 0;
+      blk(stage, Dl, D, D, o.wo + q0 * D, D, 0);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.wo, Dl * D, c->stream) ? RT_ERR_CUDA : 0;
+      blk(stage, D, Hl, 2 * Hl, o.w13, 2 * H, h0);
+      blk(stage + Hl, D, Hl, 2 * Hl, o.w13, 2 * H, H + h0);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.w13, D * 2 * Hl, c->stream) ? RT_ERR_CUDA : 0;
+      blk(stage, D, Hl, Hl, o.w2, H, h0);
+      if (!rc) rc = rt::cast_bf16(stage, c->params_bf16 + ob.w2, D * Hl, c->stream) ? RT_ERR_CUDA : 0;
+      if (!rc) rc = cudaStreamSynchronize(c->stream) ? RT_ERR_CUDA : 0;
     }
-    cudaStreamSynchronize(c->stream);
     cudaFree(stage);
+    if (rc) return set_err(c, RT_ERR_CUDA, "init normal (forward-only)");
   }
+  c->weights_set = true;
   (void)D;
   RT_CUDA(cudaStreamSynchronize(c->stream), "init sync");
   return RT_OK;
@@ -1068,7 +1194,7 @@ RT_API int rt_forward(rt_ctx* c, const uint32_t* tokens, const uint32_t* targets
   if ((rc = wait_stream(c))) return rc;
   if (loss_out) *loss_out = c->h_loss[0];
   if (per_token_loss)
-    RT_CUDA(cudaMemcpy(per_token_loss, c->row_loss, sizeof(float) * batch * c->cfg.seq, cudaMemcpyDeviceToHost),
+    RT_CUDA(cudaMemcpyAsync(per_token_loss, c->row_loss, sizeof(float) * batch * c->cfg.seq, cudaMemcpyDeviceToHost, c->stream),
             "per-token loss");
   if (!std::isfinite(c->h_loss[0])) return set_err(c, RT_ERR_NONFINITE, "loss is not finite");
   return RT_OK;
@@ -1082,12 +1208,12 @@ RT_API int rt_logits_download(rt_ctx* c, float* logits) {
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   if (c->last_softcap > 0.f) {  // report the capped logits, as the reference stores them
     std::vector<float> h(M * V);
-    RT_CUDA(cudaMemcpy(h.data(), c->logits, sizeof(float) * M * V, cudaMemcpyDeviceToHost), "logits");
+    RT_CUDA(cudaMemcpyAsync(h.data(), c->logits, sizeof(float) * M * V, cudaMemcpyDeviceToHost, c->stream), "logits");
     const float sc = c->last_softcap;
     for (int64_t i = 0; i < M * V; ++i) logits[i] = sc * tanhf(h[i] * (1.0f / sc));
     return RT_OK;
   }
-  RT_CUDA(cudaMemcpy(logits, c->logits, sizeof(float) * M * V, cudaMemcpyDeviceToHost), "logits");
+  RT_CUDA(cudaMemcpyAsync(logits, c->logits, sizeof(float) * M * V, cudaMemcpyDeviceToHost, c->stream), "logits");
   return RT_OK;
 }
 
@@ -1257,8 +1383,22 @@ RT_API int rt_nccl_unique_id(uint8_t* out128) {
 RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms) {
   if (!c || world <= 0 || rank < 0 || rank >= world) return RT_ERR_ARG;
   if (mode != RT_DIST_DATA_PARALLEL && mode != RT_DIST_TENSOR_PARALLEL) return RT_ERR_ARG;
-  if (mode == RT_DIST_TENSOR_PARALLEL)
-    return set_err(c, RT_ERR_STATE, "tensor-parallel contexts are not supported by this build");
+  if (mode == RT_DIST_TENSOR_PARALLEL) {
+    // shard heads (uneven split allowed) and hidden columns (64-column units) over the ranks
+    if (!forward_only(c)) return set_err(c, RT_ERR_STATE, "tensor parallelism needs a forward-only context");
+    if (c->weights_set) return set_err(c, RT_ERR_STATE, "call rt_dist_init before uploading or initialising weights");
+    const int nh = c->cfg.heads, units = c->cfg.hidden / 64;
+    if (world > nh || world > units) return set_err(c, RT_ERR_SHAPE, "more tensor-parallel ranks than heads");
+    const int hb = nh / world, hr = nh % world, ub = units / world, ur = units % world;
+    free_shard_buffers(c);
+    c->tp = world > 1;
+    c->heads_loc = hb + (rank < hr ? 1 : 0);
+    c->head0 = rank * hb + std::min(rank, hr);
+    c->hid_loc = 64 * (ub + (rank < ur ? 1 : 0));
+    c->hid0 = 64 * (rank * ub + std::min(rank, ur));
+    layout_bf16(c);
+    if (!alloc_shard_buffers(c)) return set_err(c, RT_ERR_OOM, "tensor-parallel shard allocation");
+  }
   c->world = world;
   c->rank = rank;
   c->dist_mode = mode;

@@ -129,7 +129,16 @@ struct rt_ctx {
   float last_softcap = 0.f;
   int64_t device_bytes = 0;
   int64_t h2d_bytes_last = 0;
-  std::vector<void*> allocations;
+  std::vector<std::pair<void*, size_t>> allocations;
+
+  // tensor parallelism (forward-only contexts): this rank's heads [head0, head0 + heads_loc)
+  // and hidden columns [hid0, hid0 + hid_loc); without TP they are all heads / columns
+  bool tp = false;
+  int heads_loc = 0, head0 = 0, hid_loc = 0, hid0 = 0;
+  std::vector<rt::LayerOffsets> layer_off_b;  // bf16 weight arena offsets (this rank's shard shapes)
+  int64_t n_bf16 = 0;
+  rt::bf16* tp_partial = nullptr;  // [M, D] bf16 partial sum of a row-parallel GEMM
+  bool weights_set = false;
 
   // distributed
   int world = 1, rank = 0, dist_mode = -1, timeout_ms = 0;

@@ -254,3 +254,20 @@ def test_timings_query_leaves_no_cuda_error():
     t = k.timings()
     assert t["fwd_ms"] > 0 and t["bwd_ms"] > 0 and t["comm_ms"] == 0
     k.train_step(tok, tgt, 1, TrainConfig())  # the next launch must still succeed
+
+
+def test_forward_only_context_matches_training_context():
+    """RT_CTX_FORWARD_ONLY (bf16 weights, reused activations) gives the same loss bits as a
+    training context, for host-uploaded and for seeded device-initialised weights."""
+    cfg = SMALL
+    w = ModelTensors.normal(cfg, seed=21, std=0.02)
+    tok, tgt = seeded(cfg, 2, seed=22)
+    kt = CompiledKernels.compile(cfg, max_batch=2)
+    kf = CompiledKernels.compile(cfg, max_batch=2, forward_only=True)
+    assert kf.device_bytes() < kt.device_bytes()
+    assert full_model.forward(cfg, kt, w, tok, tgt) == full_model.forward(cfg, kf, w, tok, tgt)
+    kt.init_normal(seed=5, std=0.02)
+    kf.init_normal(seed=5, std=0.02)
+    a, pa = kt.forward(tok, tgt, per_token=True)
+    b, pb = kf.forward(tok, tgt, per_token=True)
+    assert a == b and np.array_equal(pa, pb)
