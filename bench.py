@@ -1,16 +1,19 @@
 #!/usr/bin/env python
-"""Benchmark of rustane's language-model train step on B200.
+"""Benchmark of rustane's language-model step on B200.
 
-Workload: the 600M-class decoder (dim 1536, SwiGLU hidden
-4096, 20 layers, 12 heads x 128, seq 512, vocab 8192), per-GPU batch 8 of
+Default workload: the 600M-class decoder (dim 1536, SwiGLU
+hidden 4096, 20 layers, 12 heads x 128, seq 512, vocab 8192), per-GPU batch 8 of
 uniform-random token ids, weights N(0, 0.02) from seed 1234, fp32 master
 weights + AdamW state with bf16 compute.  One step = forward + cross-entropy +
 backward + [data-parallel gradient all-reduce] + grad-norm clip + AdamW.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 600m|5b|7b|30b] [--batch B]
 
-Under torchrun (N > 1) each rank drives one GPU; time is the max over ranks.
-Prints ONE JSON line on rank 0.
+The other BASELINE configs: `5b` trains (per-GPU batch 4, data parallel);
+`7b` (batch 1 or 16) and `30b` (batch 8) run forward + loss only, tensor
+parallel over the N GPUs.  Under torchrun (N > 1) each rank drives one GPU;
+time is the max over ranks.  Prints ONE JSON line on rank 0.
 """
 from __future__ import annotations
 
@@ -31,7 +34,13 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "train-step tok/s & forward ms at 600M/5B/7B; TC util vs B200 bf16 peak"
-PUBLISHED_TOK_S = 533.0  # 600m-A train step, M4 Max ANE + CPU (results/2026-03-18_1830_param-sweep.md:37)
+# Published reference throughput (Apple M4 Max, ANE + CPU), tok/s at batch 1:
+PUBLISHED = {
+    "600m": (533.0, "600m-A train step 533 tok/s (results/2026-03-18_1830_param-sweep.md:37)"),
+    "5b": (74.0, "5b-B train step 74 tok/s (results/2026-03-18_1830_param-sweep.md:78)"),
+    "7b": (512 / 3.132, "7B forward 3132 ms for 512 tokens (README.md:70)"),
+}
+PUBLISHED_TOK_S = PUBLISHED["600m"][0]
 SPEC_BF16_TFLOPS = 2250.0
 PER_GPU_BATCH = 8
 SEED_WEIGHTS = 1234
@@ -46,14 +55,23 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
 
 
-def workload_cfg():
+WORKLOADS = {  # name -> (ModelConfig preset, trains?, default batch, label)
+    "600m": ("c600m", True, 8, "600M train step"),
+    "5b": ("c5b", True, 4, "5B train step"),
+    "7b": ("c7b", False, 1, "7B forward + loss"),
+    "30b": ("c30b", False, 8, "30B forward + loss"),
+}
+
+
+def workload_cfg(name: str = "600m"):
     from rustane_b200 import ModelConfig
-    return ModelConfig.c600m()
+    return getattr(ModelConfig, WORKLOADS[name][0])()
 
 
-def workload_desc(cfg) -> str:
-    return (f"600M train step: dim {cfg.dim}, SwiGLU hidden {cfg.hidden}, {cfg.nlayers} layers, {cfg.heads} heads x "
-            f"{cfg.hd}, seq {cfg.seq}, vocab {cfg.vocab}, per-GPU batch {PER_GPU_BATCH}")
+def workload_desc(cfg, name: str = "600m", batch: int = PER_GPU_BATCH) -> str:
+    per = "per-GPU batch" if WORKLOADS[name][1] else "batch"
+    return (f"{WORKLOADS[name][3]}: dim {cfg.dim}, SwiGLU hidden {cfg.hidden}, {cfg.nlayers} layers, {cfg.heads} "
+            f"heads x {cfg.hd}, seq {cfg.seq}, vocab {cfg.vocab}, {per} {batch}")
 
 
 # --------------------------------------------------------------- clocks
@@ -169,6 +187,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="600m", choices=list(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=0)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -191,16 +211,19 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
 
-    cfg = workload_cfg()
-    B, S = PER_GPU_BATCH, cfg.seq
-    k = CompiledKernels.compile(cfg, max_batch=B, device=local)
-    k.init_normal(seed=SEED_WEIGHTS, std=0.02)
-    if world > 1:
+    wl = args.workload
+    train = WORKLOADS[wl][1]
+    cfg = workload_cfg(wl)
+    B, S = (args.batch or WORKLOADS[wl][2]), cfg.seq
+    k = CompiledKernels.compile(cfg, max_batch=B, device=local, forward_only=not train)
+    if world > 1:  # tensor-parallel shards must be set before the weights exist
         uid = [CompiledKernels.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        k.dist_init(world, rank, uid[0], _lib.RT_DIST_DATA_PARALLEL, timeout_ms=120000)
+        mode = _lib.RT_DIST_DATA_PARALLEL if train else _lib.RT_DIST_TENSOR_PARALLEL
+        k.dist_init(world, rank, uid[0], mode, timeout_ms=120000)
+    k.init_normal(seed=SEED_WEIGHTS, std=0.02)
 
-    rng = np.random.default_rng(1000 + rank)
+    rng = np.random.default_rng(1000 + (rank if train else 0))  # TP ranks share the batch
     nslots = 4
     batches = []
     for slot in range(nslots):
@@ -217,7 +240,10 @@ def main() -> None:
     def staged_steps(n):
         nonlocal step
         for _ in range(n):
-            k._check(L.rt_train_step_staged(k.handle, step % nslots, step, ctypes.byref(c_tc), None))
+            if train:
+                k._check(L.rt_train_step_staged(k.handle, step % nslots, step, ctypes.byref(c_tc), None))
+            else:
+                k._check(L.rt_forward_staged(k.handle, step % nslots, ctypes.c_float(0.0)))
             step += 1
 
     def barrier():
@@ -256,7 +282,7 @@ def main() -> None:
     ms = max_over_ranks(ms_local)
     launches = k.timings()["kernel_launches"] - launches0
     ms_per_step = ms / K
-    tokens = world * B * S * K
+    tokens = (world if train else 1) * B * S * K  # tensor-parallel ranks share one batch
     value = tokens / (ms / 1e3)
 
     # -------- the same steps again with a CUDA event pair around every kernel
@@ -277,7 +303,10 @@ def main() -> None:
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(K):
-        k.train_step(host_tok[i % nslots], host_tgt[i % nslots], step, tc)
+        if train:
+            k.train_step(host_tok[i % nslots], host_tgt[i % nslots], step, tc)
+        else:
+            k.forward(host_tok[i % nslots], host_tgt[i % nslots])
         step += 1
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     L.rt_last_h2d_bytes(k.handle, ctypes.byref(h2d))
@@ -287,7 +316,8 @@ def main() -> None:
     pk = peaks()
     gemm_tflops = tm["gemm_flops"] / (tm["gemm_ms"] * 1e-3) / 1e12 if tm["gemm_ms"] > 0 else None
     per_launch_flops = tm["gemm_flops"] / max(tm["gemm_launches"], 1)
-    model_flops = 3.0 * cfg.flops_per_token_fwd() * B * S  # per GPU per step (train = 3 x forward)
+    # per GPU per step: train = 3 x forward (data parallel); forward shared by the TP ranks
+    model_flops = (3.0 * cfg.flops_per_token_fwd() * B * S) if train else cfg.flops_per_token_fwd() * B * S / world
     step_tflops = model_flops / (ms_per_step * 1e-3) / 1e12
     traffic = None
     tfile = ROOT / "profiles" / "gemm_traffic.json"
@@ -296,11 +326,13 @@ def main() -> None:
 
     result = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": workload_desc(cfg), "per_gpu_batch": B, "seq_len": S, "tokens_per_gpu_step": B * S,
-                   "parallelism": f"dp{world}", "weights": "N(0,0.02) seed 1234, fp32 master + AdamW state",
-                   "tokens": "uniform ids, seed 1000+rank",
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak" if train else "strong",
+        "vs_baseline": (value / PUBLISHED[wl][0]) if wl in PUBLISHED else None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": workload_desc(cfg, wl, B), "per_gpu_batch": B, "seq_len": S,
+                   "tokens_per_gpu_step": B * S, "parallelism": (f"dp{world}" if train else f"tp{world}"),
+                   "weights": ("N(0,0.02) seed 1234, fp32 master + AdamW state" if train
+                               else "N(0,0.02) seed 1234, bf16"),
+                   "tokens": "uniform ids, seed 1000+rank" if train else "uniform ids, seed 1000",
                    "l2": "not flushed: every step streams > 10 GB of weights/grads/optimizer state (>> 126 MB L2)"},
         "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM (all projections, FFN, logits, data and weight grads)",
                      "achieved": gemm_tflops, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
@@ -319,9 +351,11 @@ def main() -> None:
         "kernel_ms_per_step": {"gemm": tm["gemm_ms"] / KP, "attention": tm["attn_ms"] / KP,
                                "other": tm["other_ms"] / KP, "profiled_steps": KP},
         "loss_last": loss_last.value,
-        "vs_baseline_basis": "600m-A train step 533 tok/s, Apple M4 Max (BASELINE.md)",
+        "vs_baseline_basis": (PUBLISHED[wl][1] + ", Apple M4 Max") if wl in PUBLISHED else None,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if not train:
+        result["fwd_ms"] = ms_per_step
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and wl == "600m":
         times, threads, blas = oracle_step_seconds(cfg, 2, budget_s=25.0)
         per = statistics.mean(times)
         result["cpu_baseline"] = {"value": cfg.seq / per, "unit": "tok/s", "cores": threads, "kind": "port",
