@@ -219,7 +219,10 @@ RT_API int rt_get_timings(rt_ctx* ctx, rt_timings* out);
  * Replaces the DynMatmul / DualDynMatmul ANE graphs
  * (crates/engine/src/kernels/dyn_matmul.rs:15-86), the matmuls inside
  * sdpaFwd/ffnFused (kernels/sdpa_fwd.rs:80-83, kernels/ffn_fused.rs:48-72) and
- * the cblas_sgemm calls (crates/engine/src/cpu/vdsp.rs:128-136, :287-321). */
+ * the cblas_sgemm calls (crates/engine/src/cpu/vdsp.rs:128-136, :287-321).
+ * force_bn: 0 lets the library choose; 128/192/256 force the single-CTA kernel
+ * with that output tile width; -256/-128 force the CTA-pair kernel (a cluster
+ * of two SMs owns a 256 x 256 / 256 x 128 tile). */
 RT_API int rt_kernel_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int M, int N,
                           int K, int epi, void* out, int64_t ldo, void* out2, int64_t ldo2, const void* aux,
                           int64_t ld_aux, float alpha, int beta, const float* rope_cos, const float* rope_sin,

@@ -33,6 +33,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 B = one swizzle row
 
 constexpr int kEpiWarps = 8;                    // warps 4..11: two per TMEM lane quadrant
+constexpr int kRasterGroup = 16;                // M-tiles (of 128 rows) per raster band
 constexpr int kThreads = 128 + 32 * kEpiWarps;  // + producer, MMA, allocator, spare
 
 template <int BN>
@@ -63,6 +64,20 @@ struct KParams {
   const float* rope_sin;
   int* err;
 };
+
+// Tile order: groups of `group` M-tiles; inside a group M runs fastest, then N.
+// The CTAs resident at one time then share a band of A rows and a few B column
+// tiles, so operands larger than L2 are read from HBM about once instead of
+// once per N tile (with M running fastest over all of M, every wave would
+// stream all of A).  With num_m <= group this is plain M-fastest order.
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group, int& tm, int& tn) {
+  const int band = tile / (group * num_n);
+  const int m_first = band * group;
+  const int gm = min(num_m - m_first, group);
+  const int r = tile - band * group * num_n;
+  tm = m_first + r % gm;
+  tn = r / gm;
+}
 
 __device__ __forceinline__ float silu_sigmoid(float x, float& sig) {
   sig = 1.f / (1.f + __expf(-x));
@@ -315,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;  // stages armed so far
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int tm = tile % p.num_m, tn = tile / p.num_m;
+        int tm, tn;
+        tile_coords(tile, p.num_m, p.num_n, kRasterGroup, tm, tn);
         const int m0 = tm * BM;
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int stage = it % C::STAGES;
@@ -417,7 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (local >> 1) & 1;
-      const int tm = tile % p.num_m, tn = tile / p.num_m;
+      int tm, tn;
+      tile_coords(tile, p.num_m, p.num_n, kRasterGroup, tm, tn);
       const int m = tm * BM + q * 32 + lane;
       AuxRegs pre;  // first chunk's auxiliary inputs do not depend on the MMA: fetch before waiting
       if constexpr (EPI != kEpiSwiglu) {
@@ -448,6 +465,227 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------- CTA-pair kernel
+// Same pipeline as above, but a cluster of two CTAs computes a 256 x BN tile
+// with tcgen05.mma.cta_group::2: each CTA loads its own 128 rows of A and its
+// own half of the B columns into its own shared memory (completion bytes
+// counted on the leader's barrier), the leader (cluster rank 0) issues the
+// MMAs, which read both CTAs' shared memory and write each CTA's 128 rows of
+// the accumulator into that CTA's TMEM; both CTAs run the epilogue on their rows.
+// Per SM this halves the B tile traffic for the same math.
+template <int BN>
+struct Gemm2Cfg {
+  static constexpr int BNH = BN / 2;  // B columns held by each CTA
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = BNH * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 6 : 8;
+  static constexpr int ACC_STRIDE = BN;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const KParams p) {
+  using C = Gemm2Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* tfull_bar = empty_bar + C::STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * kEpiWarps);  // epilogue warps of both CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {  // same warp in both CTAs, same slot offset
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_m2 = (p.M + 255) / 256;
+  const int num_tiles = num_m2 * p.num_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer (both CTAs)
+      int it = 0;
+      bool ok = true;
+      const uint32_t full0 = mapa_shared(smem_u32(&full_bar[0]), 0);  // the leader's barriers
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        int tm, tn;
+        tile_coords(tile, num_m2, p.num_n, kRasterGroup / 2, tm, tn);
+        const int m0 = tm * 256 + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int stage = it % C::STAGES;
+          const uint32_t phase = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1) || *abort_flag) {
+            set_error(p.err, kDevTimeoutProducer);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+          const uint32_t fbar = full0 + 8 * stage;
+          const int k0 = kb * BK;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(sA + j * 8192, &tmA, fbar, m0 + 64 * j, k0);
+          } else {
+            tma_load_2d_pair(sA, &tmA, fbar, k0, m0);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < C::BNH / 64; ++j) {
+              const int lc = static_cast<int>(rank) * C::BNH + 64 * j;  // column within the tile
+              int nphys;
+              if constexpr (EPI == kEpiSwiglu) {
+                constexpr int HALF = BN / 2;  // rank 0 holds the W1 columns, rank 1 the W3 columns
+                nphys = (lc < HALF) ? tn * HALF + lc : p.n_half + tn * HALF + (lc - HALF);
+              } else {
+                nphys = tn * BN + lc;
+              }
+              tma_load_2d_pair(sB + j * 8192, &tmB, fbar, nphys, k0);
+            }
+          } else {
+            tma_load_2d_pair(sB, &tmB, fbar, k0, tn * BN + static_cast<int>(rank) * C::BNH);
+          }
+        }
+      }
+      if (!ok && leader) {  // the leader's full barriers also count the peer's copies
+        for (int i = (it > C::STAGES ? it - C::STAGES : 0); i < it; ++i)
+          mbar_wait(&full_bar[i % C::STAGES], (i / C::STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------------------------------------------------- MMA issuer (leader)
+      constexpr uint32_t idesc = idesc_bf16_f32(256, BN, A_MN, B_MN);
+      // the same barrier offsets in the peer CTA (cluster rank 1)
+      const uint32_t empty0 = smem_u32(&empty_bar[0]), empty1 = mapa_shared(empty0, 1);
+      const uint32_t tfull0 = smem_u32(&tfull_bar[0]), tfull1 = mapa_shared(tfull0, 1);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_par = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_par ^ 1) || *abort_flag) {
+          set_error(p.err, kDevTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int stage = it % C::STAGES;
+          const uint32_t phase = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full_bar[stage], phase) || *abort_flag) {
+            set_error(p.err, kDevTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(empty0 + 8 * stage);  // both CTAs' slots are free once these finish
+          umma_commit_pair(empty1 + 8 * stage);
+        }
+        if (ok) {
+          umma_commit_pair(tfull0 + 8 * acc);
+          umma_commit_pair(tfull1 + 8 * acc);
+        }
+      }
+      umma_commit_pair(smem_u32(drain_bar));
+      mbar_wait(drain_bar, 0);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    constexpr int NCH = (EPI == kEpiSwiglu) ? (BN / 2) / 32 : BN / 32;
+    const int c0 = half * NCH / 2, c1 = (half + 1) * NCH / 2;
+    const uint32_t tempty0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);  // the leader's barriers
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_par = (local >> 1) & 1;
+      int tm, tn;
+      tile_coords(tile, num_m2, p.num_n, kRasterGroup / 2, tm, tn);
+      const int m = tm * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      AuxRegs pre;
+      if constexpr (EPI != kEpiSwiglu) {
+        const int n0 = tn * BN + c0 * 32;
+        if (c0 < c1) load_aux<EPI>(p, static_cast<int64_t>(m), n0, m < p.M && n0 < p.N, pre);
+      }
+      bool ok = mbar_wait(&tfull_bar[acc], acc_par);
+      ok = __all_sync(0xffffffffu, ok);
+      const int aborted = __shfl_sync(0xffffffffu, *abort_flag, 0);
+      if (!ok || aborted) {
+        if (!ok && lane == 0) {
+          set_error(p.err, kDevTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tbase =
+          tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE) + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue_tile<BN, EPI>(p, tbase, m, tn, c0, c1, pre);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + 8 * acc);
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into this CTA's TMEM and both epilogues are done
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -489,32 +727,45 @@ int launch_inst(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
   return cudaGetLastError();
 }
 
+template <int BN, bool A_MN, bool B_MN, int EPI>
+int launch_inst2(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid, cudaStream_t s) {
+  using C = Gemm2Cfg<BN>;
+  static const cudaError_t attr = cudaFuncSetAttribute(gemm_tc2_kernel<BN, A_MN, B_MN, EPI>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (attr != cudaSuccess) return attr;
+  gemm_tc2_kernel<BN, A_MN, B_MN, EPI><<<grid, kThreads, C::SMEM_BYTES, s>>>(ta, tb, kp);
+  return cudaGetLastError();
+}
+
+// Every (A major, B major, epilogue) combination the LM step launches.
+#define RT_GEMM_COMBOS(X)                                                                    \
+  /* forward projections (B = weight, MN-major) */                                          \
+  X(false, true, kEpiRope) X(false, true, kEpiResidual) X(false, true, kEpiSwiglu)           \
+  X(false, true, kEpiSwigluBwd) X(false, true, kEpiF32) X(false, true, kEpiBf16)             \
+  X(false, true, kEpiF32Acc)                                                                 \
+  /* K-major weights (W2 forward, logits, data gradients) */                                \
+  X(false, false, kEpiBf16) X(false, false, kEpiF32) X(false, false, kEpiF32Acc)             \
+  X(false, false, kEpiResidual) X(false, false, kEpiRope) X(false, false, kEpiSwigluBwd)     \
+  /* weight gradients: both operands contract over tokens */                                \
+  X(true, true, kEpiF32Acc) X(true, true, kEpiF32) X(true, true, kEpiBf16)                   \
+  X(true, false, kEpiF32) X(true, false, kEpiF32Acc)
+
+template <int BN>
+int dispatch2(const GemmArgs& g, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+              cudaStream_t s) {
+#define RT_GEMM_CASE(AMN, BMN, EPI) \
+  if (g.a_mn == AMN && g.b_mn == BMN && g.epi == EPI) return launch_inst2<BN, AMN, BMN, EPI>(ta, tb, kp, grid, s);
+  RT_GEMM_COMBOS(RT_GEMM_CASE)
+#undef RT_GEMM_CASE
+  return -1;
+}
+
 template <int BN>
 int dispatch(const GemmArgs& g, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
              cudaStream_t s) {
 #define RT_GEMM_CASE(AMN, BMN, EPI) \
   if (g.a_mn == AMN && g.b_mn == BMN && g.epi == EPI) return launch_inst<BN, AMN, BMN, EPI>(ta, tb, kp, grid, s);
-  // forward projections (B = weight, MN-major)
-  RT_GEMM_CASE(false, true, kEpiRope)
-  RT_GEMM_CASE(false, true, kEpiResidual)
-  RT_GEMM_CASE(false, true, kEpiSwiglu)
-  RT_GEMM_CASE(false, true, kEpiSwigluBwd)
-  RT_GEMM_CASE(false, true, kEpiF32)
-  RT_GEMM_CASE(false, true, kEpiBf16)
-  RT_GEMM_CASE(false, true, kEpiF32Acc)
-  // K-major weights (W2 forward, logits, data gradients)
-  RT_GEMM_CASE(false, false, kEpiBf16)
-  RT_GEMM_CASE(false, false, kEpiF32)
-  RT_GEMM_CASE(false, false, kEpiF32Acc)
-  RT_GEMM_CASE(false, false, kEpiResidual)
-  RT_GEMM_CASE(false, false, kEpiRope)
-  RT_GEMM_CASE(false, false, kEpiSwigluBwd)
-  // weight gradients: both operands contract over tokens
-  RT_GEMM_CASE(true, true, kEpiF32Acc)
-  RT_GEMM_CASE(true, true, kEpiF32)
-  RT_GEMM_CASE(true, true, kEpiBf16)
-  RT_GEMM_CASE(true, false, kEpiF32)
-  RT_GEMM_CASE(true, false, kEpiF32Acc)
+  RT_GEMM_COMBOS(RT_GEMM_CASE)
 #undef RT_GEMM_CASE
   return -1;
 }
@@ -533,6 +784,56 @@ int num_sms() {
   return g_num_sms;
 }
 
+namespace {
+
+// CTA-pair path: the cluster of two CTAs owns a 256 x bn output tile.
+int gemm_launch_pair(const GemmArgs& g, int bn, cudaStream_t stream) {
+  const bool swiglu = g.epi == kEpiSwiglu;
+  if (swiglu && g.N % (bn / 2) != 0) return -1;
+  KParams kp{};
+  kp.M = g.M;
+  kp.N = g.N;
+  kp.num_kb = g.K / BK;
+  kp.num_m = (g.M + 255) / 256;
+  kp.num_n = swiglu ? g.N / (bn / 2) : (g.N + bn - 1) / bn;
+  kp.num_tiles = kp.num_m * kp.num_n;
+  kp.n_half = g.n_half;
+  kp.beta = g.beta;
+  kp.alpha = g.alpha;
+  kp.seq = g.seq;
+  kp.rope_cols = g.rope_cols;
+  kp.out = g.out;
+  kp.ldo = g.ldo;
+  kp.out2 = g.out2;
+  kp.ldo2 = g.ldo2;
+  kp.aux = g.aux;
+  kp.ld_aux = g.ld_aux;
+  kp.rope_cos = g.rope_cos;
+  kp.rope_sin = g.rope_sin;
+  kp.err = g.err;
+
+  CUtensorMap ta, tb;
+  bool ok;
+  if (g.a_mn)
+    ok = make_tmap(&ta, g.a, g.M, g.K, g.lda, 64, 64);
+  else
+    ok = make_tmap(&ta, g.a, g.K, g.M, g.lda, 64, BM);
+  if (!ok) return -3;
+  const uint64_t b_inner_mn = swiglu ? uint64_t(g.n_half) + g.N : uint64_t(g.N);
+  if (g.b_mn)
+    ok = make_tmap(&tb, g.b, b_inner_mn, g.K, g.ldb, 64, 64);
+  else
+    ok = make_tmap(&tb, g.b, g.K, g.N, g.ldb, 64, bn / 2);
+  if (!ok) return -3;
+
+  const int max_pairs = num_sms() / 2;
+  const int grid = 2 * (kp.num_tiles < max_pairs ? kp.num_tiles : max_pairs);
+  if (bn == 256) return dispatch2<256>(g, ta, tb, kp, grid, stream);
+  return dispatch2<128>(g, ta, tb, kp, grid, stream);
+}
+
+}  // namespace
+
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (!encoder_ready()) return -2;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.K % BK != 0 || g.N % 32 != 0) return -1;
@@ -549,10 +850,15 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     const int per_tile_n = swiglu ? bn / 2 : bn;
     return ((g.M + BM - 1) / BM) * ((g.N + per_tile_n - 1) / per_tile_n);
   };
+  // force_bn: 128/192/256 pick the single-CTA kernel with that tile width,
+  // -256/-128 the CTA-pair kernel (256-row tiles); anything else chooses.
+  if (g.force_bn == -256 || g.force_bn == -128) return gemm_launch_pair(g, -g.force_bn, stream);
   int bn = g.force_bn;
   if (bn != 128 && bn != 192 && bn != 256) {
     // time ~ waves x tile width / efficiency: 128-wide tiles are closer to the
-    // shared-memory read limit (A is re-read per 128 columns), 256 is the best.
+    // shared-memory read limit (A is re-read per 128 columns), 256 is the best
+    // single-CTA width, and the CTA pair's 256 x 256 tile (half the B traffic
+    // per SM) measured 2-8% faster than it at equal wave counts.
     double best = 1e30;
     for (int cand : {256, 192, 128}) {
       if (swiglu && (cand == 192 || g.N % (cand / 2) != 0)) continue;
@@ -563,6 +869,12 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
         best = cost;
         bn = cand;
       }
+    }
+    if (!swiglu || g.N % 128 == 0) {
+      const int pairs = sms / 2;
+      const int t2 = ((g.M + 255) / 256) * (swiglu ? g.N / 128 : (g.N + 255) / 256);
+      const double cost2 = double((t2 + pairs - 1) / pairs) * 256 / 1.04;
+      if (cost2 < best * 0.999) return gemm_launch_pair(g, 256, stream);
     }
   }
   if (swiglu && (bn == 192 || g.N % (bn / 2) != 0)) bn = 128;

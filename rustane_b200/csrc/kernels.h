@@ -43,7 +43,7 @@ struct GemmArgs {
   int rope_cols = 0;
   int n_half = 0;  // kEpiSwiglu / kEpiSwigluBwd: column offset of the h3 / dh3 half
   int* err = nullptr;
-  int force_bn = 0;  // 0: choose tile width from the wave count; 128 or 256 to force
+  int force_bn = 0;  // 0: choose from the wave count; 128/192/256 force a 1-CTA tile width, -256/-128 the CTA-pair kernel
 };
 
 // Returns a cudaError_t-compatible code (0 = launched) or -1 on bad arguments.

@@ -1,6 +1,6 @@
 """Single-kernel timing of the LM-step kernels at a chosen shape (CUDA events).
 
-    python -m rustane_b200.kernel_bench gemm --m 4096 --n 4096 --k 1536 --b-mn --epi swiglu
+    python -m rustane_b200.kernel_bench gemm --m 4096 --n 4096 --k 1536 --b-mn --epi swiglu [--bn -256 | --cublas]
     python -m rustane_b200.kernel_bench attention --batch 8 --seq 512 --heads 12 [--bwd]
     python -m rustane_b200.kernel_bench rmsnorm_bwd --m 4096 --d 1536
 
@@ -66,11 +66,19 @@ def bench_gemm(args):
                               N if epi in (_lib.EPI_SWIGLU, _lib.EPI_SWIGLU_BWD) else 0, args.bn, err.data_ptr(), st)
         assert rc == 0, rc
 
+    flops = 2.0 * M * ncols * K
+    if args.cublas:
+        # the same operands through torch.matmul (cuBLAS), bf16 output: a library
+        # reference point for the mainloop, without our fused epilogue
+        A_log = A.t() if args.a_mn else A
+        B_log = B if args.b_mn else B.t()
+        C = torch.empty(M, ncols, device="cuda", dtype=torch.bfloat16)
+        us = _time(lambda: torch.matmul(A_log, B_log, out=C), args.iters)
+        return {"kernel": "cublas_bf16", "M": M, "N": ncols, "K": K, "us": us, "tflops": flops / us / 1e6}
     us = _time(run, args.iters)
     assert err.item() == 0
-    flops = 2.0 * M * ncols * K
     return {"kernel": "gemm", "M": M, "N": N, "K": K, "epi": args.epi, "a_mn": args.a_mn, "b_mn": args.b_mn,
-            "us": us, "tflops": flops / us / 1e6}
+            "bn": args.bn, "us": us, "tflops": flops / us / 1e6}
 
 
 def bench_attention(args):
@@ -130,7 +138,8 @@ def main():
     ap.add_argument("--b-mn", action="store_true")
     ap.add_argument("--epi", default="f32", choices=list(EPIS))
     ap.add_argument("--beta", type=int, default=0)
-    ap.add_argument("--bn", type=int, default=0)
+    ap.add_argument("--bn", type=int, default=0, help="0 auto; 128/192/256 single-CTA; -256/-128 CTA pair")
+    ap.add_argument("--cublas", action="store_true", help="time torch.matmul on the same operands instead")
     ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--heads", type=int, default=12)

@@ -1,7 +1,8 @@
 """tcgen05 GEMM parity on the GPU against a plain torch fp32 matmul.
 
-Covers every operand-major combination (K-major / MN-major for A and B), both
-tile widths, ring wrap-around (K > stages * 64), persistent CTAs with more tiles
+Covers every operand-major combination (K-major / MN-major for A and B), the
+single-CTA kernel at each tile width and the CTA-pair kernel (force_bn -256 /
+-128: two SMs of a cluster own a 256-row tile), ring wrap-around (K > stages * 64), persistent CTAs with more tiles
 than SMs (TMEM double buffer), ragged M/N edges, and each fused epilogue the LM
 step uses.  Inputs are bf16; the reference multiplies the same bf16 values in
 fp32, so only accumulation order differs (tolerance 1e-4 normwise).
@@ -60,8 +61,11 @@ def _no_tf32():
     torch.backends.cuda.matmul.allow_tf32 = False
 
 
+PAIR = [-256, -128]
+
+
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 192, 256] + PAIR)
 def test_gemm_majors_f32(a_mn, b_mn, bn):
     M, N, K = 256, 512, 448
     A, B, ref = operands(M, N, K, a_mn, b_mn)
@@ -70,7 +74,7 @@ def test_gemm_majors_f32(a_mn, b_mn, bn):
     assert _rel(out, ref) < TOL
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256] + PAIR)
 def test_gemm_persistent_many_tiles(bn):
     # more tiles than SMs: every CTA cycles both TMEM accumulators several times
     M, N, K = 2048, 4096, 256
@@ -80,52 +84,61 @@ def test_gemm_persistent_many_tiles(bn):
     assert _rel(out, ref) < TOL
 
 
-def test_gemm_ragged_edges():
-    # M not a multiple of 128 and N not a multiple of the tile width
-    M, N, K = 200, 352, 192
+@pytest.mark.parametrize("bn", [0] + PAIR)
+@pytest.mark.parametrize("M", [200, 328])
+def test_gemm_ragged_edges(bn, M):
+    # M not a multiple of the tile height and N not a multiple of the tile width;
+    # rows past M must stay untouched
+    N, K = 352, 192
     A, B, ref = operands(M, N, K, False, False, seed=2)
-    out = torch.full((M, N), 7.0, device="cuda")
-    gemm(A, False, B, False, M, N, K, _lib.EPI_F32, out)
-    assert _rel(out, ref) < TOL
+    out = torch.full((M + 8, N), 7.0, device="cuda")
+    gemm(A, False, B, False, M, N, K, _lib.EPI_F32, out, force_bn=bn)
+    assert _rel(out[:M], ref) < TOL
+    assert bool((out[M:] == 7.0).all())
 
 
-def test_gemm_bf16_out():
+@pytest.mark.parametrize("bn", [0] + PAIR)
+def test_gemm_bf16_out(bn):
     M, N, K = 384, 768, 512
     A, B, ref = operands(M, N, K, False, True, seed=3)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    gemm(A, False, B, True, M, N, K, _lib.EPI_BF16, out)
+    gemm(A, False, B, True, M, N, K, _lib.EPI_BF16, out, force_bn=bn)
     assert _rel(out, ref) < 8e-3
 
 
+@pytest.mark.parametrize("bn", [0] + PAIR)
 @pytest.mark.parametrize("beta", [0, 1])
-def test_gemm_f32_accumulate(beta):
+def test_gemm_f32_accumulate(beta, bn):
     M, N, K = 256, 384, 1024
     A, B, ref = operands(M, N, K, True, True, seed=4)
     out = torch.randn(M, N, device="cuda")
     base = out.clone()
-    gemm(A, True, B, True, M, N, K, _lib.EPI_F32_ACC, out, beta=beta)
+    gemm(A, True, B, True, M, N, K, _lib.EPI_F32_ACC, out, beta=beta, force_bn=bn)
     expect = ref + base if beta else ref
     assert _rel(out, expect) < TOL
 
 
-def test_gemm_residual():
+@pytest.mark.parametrize("bn", [0] + PAIR)
+@pytest.mark.parametrize("b_mn", [True, False])
+def test_gemm_residual(b_mn, bn):
     M, N, K = 512, 768, 768
-    A, B, ref = operands(M, N, K, False, True, seed=5)
+    A, B, ref = operands(M, N, K, False, b_mn, seed=5)
     resid = torch.randn(M, N, device="cuda")
     out = torch.empty(M, N, device="cuda")
     alpha = 0.1581
-    gemm(A, False, B, True, M, N, K, _lib.EPI_RESIDUAL, out, aux=resid, alpha=alpha)
+    gemm(A, False, B, b_mn, M, N, K, _lib.EPI_RESIDUAL, out, aux=resid, alpha=alpha, force_bn=bn)
     assert _rel(out, resid + alpha * ref) < TOL
 
 
-def test_gemm_rope_qkv():
+@pytest.mark.parametrize("bn", [0] + PAIR)
+def test_gemm_rope_qkv(bn):
     seq, D, B = 256, 256, 2
     M, N, K = B * seq, 3 * D, 256
     A, Bw, ref = operands(M, N, K, False, True, seed=6)
     cos, sin = rope_tables(seq)
     rope = (torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda())
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    gemm(A, False, Bw, True, M, N, K, _lib.EPI_ROPE, out, rope=rope, seq=seq, rope_cols=2 * D)
+    gemm(A, False, Bw, True, M, N, K, _lib.EPI_ROPE, out, rope=rope, seq=seq, rope_cols=2 * D, force_bn=bn)
     exp = ref.clone()
     pos = torch.arange(M, device="cuda") % seq
     c = rope[0][pos].repeat(1, 2 * D // 128)  # [M, D] pairs
@@ -137,7 +150,7 @@ def test_gemm_rope_qkv():
     assert _rel(out, exp) < 8e-3
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256] + PAIR)
 def test_gemm_swiglu(bn):
     M, D, H = 512, 256, 640
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -153,14 +166,15 @@ def test_gemm_swiglu(bn):
     assert _rel(gate, torch.nn.functional.silu(h1) * h3) < 8e-3
 
 
-def test_gemm_swiglu_bwd():
+@pytest.mark.parametrize("bn", [0] + PAIR)
+def test_gemm_swiglu_bwd(bn):
     M, D, H = 256, 256, 384
     g = torch.Generator(device="cuda").manual_seed(8)
     dffn = torch.randn(M, D, generator=g, device="cuda").bfloat16()
     w2 = (0.1 * torch.randn(D, H, generator=g, device="cuda")).bfloat16()  # reference layout [D, H]
     h13 = torch.randn(M, 2 * H, generator=g, device="cuda").bfloat16()
     dh13 = torch.empty(M, 2 * H, device="cuda", dtype=torch.bfloat16)
-    gemm(dffn, False, w2, True, M, H, D, _lib.EPI_SWIGLU_BWD, dh13, aux=h13, n_half=H)
+    gemm(dffn, False, w2, True, M, H, D, _lib.EPI_SWIGLU_BWD, dh13, aux=h13, n_half=H, force_bn=bn)
     dg = dffn.float() @ w2.float()
     h1, h3 = h13[:, :H].float(), h13[:, H:].float()
     sig = torch.sigmoid(h1)
