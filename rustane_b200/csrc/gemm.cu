@@ -41,10 +41,12 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 192 ? 5 : 6);
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 192 ? 4 : 6);
   static constexpr int ACC_STRIDE = (BN == 192) ? 256 : BN;  // TMEM columns per accumulator buffer
   static constexpr int TMEM_COLS = 2 * ACC_STRIDE;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;       // epilogue transpose buffers
+  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * 32 * 128;
+  static constexpr int SMEM_BYTES = BAR_OFF + 1024 + 256;
 };
 
 struct KParams {
@@ -84,179 +86,195 @@ __device__ __forceinline__ float silu_sigmoid(float x, float& sig) {
   return x * sig;
 }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    d[q] = make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
-                      pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
-  }
+// ------------------------------------------------------------------ epilogue
+// TMEM gives each epilogue lane one accumulator row.  Writing rows straight to
+// global memory makes every warp access touch 32 different lines with 16 bytes
+// each; instead each 32 x 32 chunk is transposed through a 4 KB per-warp
+// shared-memory buffer (16-byte units XOR-swizzled by row, conflict-free both
+// ways) into the coalesced layout: lane l holds rows 4i + (l >> 3), i = 0..7,
+// columns 4 (l & 7) .. 4 (l & 7) + 3 of the chunk, so one warp access covers
+// four whole rows of the chunk.  Auxiliary inputs are loaded in the same layout.
+constexpr int kEpiBufBytes = 32 * 128;  // per epilogue warp
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 u = s[q];
-    v[8 * q + 0] = bf16lo(u.x);
-    v[8 * q + 1] = bf16hi(u.x);
-    v[8 * q + 2] = bf16lo(u.y);
-    v[8 * q + 3] = bf16hi(u.y);
-    v[8 * q + 4] = bf16lo(u.z);
-    v[8 * q + 5] = bf16hi(u.z);
-    v[8 * q + 6] = bf16lo(u.w);
-    v[8 * q + 7] = bf16hi(u.w);
-  }
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
-// Per-chunk auxiliary inputs of the epilogue (loaded one chunk ahead so their
-// global-memory latency overlaps the previous chunk's work).
+// Row of the chunk held in slot i by this lane, and the lane's first column.
+__device__ __forceinline__ int crow(int i, int lane) { return 4 * i + (lane >> 3); }
+__device__ __forceinline__ int ccol(int lane) { return 4 * (lane & 7); }
+
+// TMEM chunk (32 lanes x 32 columns at taddr) -> coalesced layout w[8].
+__device__ __forceinline__ void tmem_chunk_coalesced(uint32_t taddr, uint32_t wbuf, int lane, float4 (&w)[8]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_ld_wait();
+  const uint32_t row = wbuf + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) sts128(row + ((j ^ (lane & 7)) << 4), r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = crow(i, lane);
+    w[i] = lds128(wbuf + rr * 128 + (((lane & 7) ^ (rr & 7)) << 4));
+  }
+  __syncwarp();  // the buffer is rewritten by the next chunk
+}
+
+__device__ __forceinline__ uint2 pack_bf16x4(float4 v) { return make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w)); }
+__device__ __forceinline__ float4 unpack_bf16x4(uint32_t lo, uint32_t hi) {
+  return make_float4(bf16lo(lo), bf16hi(lo), bf16lo(hi), bf16hi(hi));
+}
+
+// Per-chunk auxiliary inputs in the coalesced layout (loaded one chunk ahead
+// so their latency overlaps the previous chunk's work).  fp32 aux: u[i] is a
+// float4; SwiGLU backward: u[i].xy = 4 bf16 of h1, u[i].zw = 4 bf16 of h3;
+// RoPE: u[i].xy = cos, u[i].zw = sin of the lane's two column pairs.
 struct AuxRegs {
   uint4 u[8];
 };
 
 template <int EPI>
-__device__ __forceinline__ void load_aux(const KParams& p, int64_t mrow, int n, bool ok, AuxRegs& a) {
-  if (!ok) return;
-  if constexpr (EPI == kEpiResidual) {
-    const uint4* r = reinterpret_cast<const uint4*>(static_cast<const float*>(p.aux) + mrow * p.ld_aux + n);
+__device__ __forceinline__ void load_aux(const KParams& p, int mbase, int n, int lane, AuxRegs& a) {
+  if (n >= p.N) return;
+  const int col = n + ccol(lane);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) a.u[q] = r[q];
-  } else if constexpr (EPI == kEpiSwigluBwd) {
-    const __nv_bfloat16* h13 = static_cast<const __nv_bfloat16*>(p.aux) + mrow * p.ld_aux;
-    const uint4* h1 = reinterpret_cast<const uint4*>(h13 + n);
-    const uint4* h3 = reinterpret_cast<const uint4*>(h13 + p.n_half + n);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      a.u[q] = h1[q];
-      a.u[4 + q] = h3[q];
-    }
-  } else if constexpr (EPI == kEpiF32Acc) {
-    if (p.beta) {
-      const uint4* r = reinterpret_cast<const uint4*>(static_cast<const float*>(p.out) + mrow * p.ldo + n);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) a.u[q] = r[q];
-    }
-  }
-}
-
-__device__ __forceinline__ void unpack_bf16x32(const uint4* u, float* v) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    v[8 * q + 0] = bf16lo(u[q].x);
-    v[8 * q + 1] = bf16hi(u[q].x);
-    v[8 * q + 2] = bf16lo(u[q].y);
-    v[8 * q + 3] = bf16hi(u[q].y);
-    v[8 * q + 4] = bf16lo(u[q].z);
-    v[8 * q + 5] = bf16hi(u[q].z);
-    v[8 * q + 6] = bf16lo(u[q].w);
-    v[8 * q + 7] = bf16hi(u[q].w);
-  }
-}
-
-// One 32-column chunk of the epilogue for accumulator row m (values v[32] are fp32 accumulators).
-template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const KParams& p, int64_t mrow, int n, float* v, const AuxRegs& a) {
-  if constexpr (EPI == kEpiBf16) {
-    store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
-  } else if constexpr (EPI == kEpiF32 || EPI == kEpiF32Acc || EPI == kEpiResidual) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + mrow * p.ldo + n);
-    if constexpr (EPI == kEpiF32Acc) {
-      if (p.beta) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 o = *reinterpret_cast<const float4*>(&a.u[q]);
-          v[4 * q + 0] += o.x;
-          v[4 * q + 1] += o.y;
-          v[4 * q + 2] += o.z;
-          v[4 * q + 3] += o.w;
-        }
-      }
-    }
+  for (int i = 0; i < 8; ++i) {
+    const int m = mbase + crow(i, lane);
+    if (m >= p.M) continue;
+    const int64_t mr = m;
     if constexpr (EPI == kEpiResidual) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 o = *reinterpret_cast<const float4*>(&a.u[q]);
-        v[4 * q + 0] = o.x + p.alpha * v[4 * q + 0];
-        v[4 * q + 1] = o.y + p.alpha * v[4 * q + 1];
-        v[4 * q + 2] = o.z + p.alpha * v[4 * q + 2];
-        v[4 * q + 3] = o.w + p.alpha * v[4 * q + 3];
+      a.u[i] = *reinterpret_cast<const uint4*>(static_cast<const float*>(p.aux) + mr * p.ld_aux + col);
+    } else if constexpr (EPI == kEpiSwigluBwd) {
+      const __nv_bfloat16* h13 = static_cast<const __nv_bfloat16*>(p.aux) + mr * p.ld_aux;
+      const uint2 h1 = *reinterpret_cast<const uint2*>(h13 + col);
+      const uint2 h3 = *reinterpret_cast<const uint2*>(h13 + p.n_half + col);
+      a.u[i] = make_uint4(h1.x, h1.y, h3.x, h3.y);
+    } else if constexpr (EPI == kEpiF32Acc) {
+      if (p.beta) a.u[i] = *reinterpret_cast<const uint4*>(static_cast<const float*>(p.out) + mr * p.ldo + col);
+    } else if constexpr (EPI == kEpiRope) {
+      if (col < p.rope_cols) {
+        const int pos = static_cast<int>(mr % p.seq);
+        const int ip = (col & 127) >> 1;
+        const uint2 c2 = *reinterpret_cast<const uint2*>(p.rope_cos + pos * 64 + ip);
+        const uint2 s2 = *reinterpret_cast<const uint2*>(p.rope_sin + pos * 64 + ip);
+        a.u[i] = make_uint4(c2.x, c2.y, s2.x, s2.y);
       }
     }
-#pragma unroll
-    for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-  } else if constexpr (EPI == kEpiRope) {
-    // Interleaved-pair rotation per head of 128 (kernels/sdpa_fwd.rs:18-33, 100-128):
-    //   y[2i] = x[2i] cos - x[2i+1] sin,  y[2i+1] = x[2i+1] cos + x[2i] sin
-    if (n < p.rope_cols) {
-      const int pos = static_cast<int>(mrow % p.seq);
-      const int i0 = (n & 127) >> 1;
-      const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + pos * 64 + i0);
-      const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + pos * 64 + i0);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 c4 = cs[q], s4 = sn[q];
-        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = 4 * q + e;
-          const float x0 = v[2 * t], x1 = v[2 * t + 1];
-          v[2 * t] = x0 * cc[e] - x1 * ss[e];
-          v[2 * t + 1] = x1 * cc[e] + x0 * ss[e];
-        }
-      }
-    }
-    store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo + n, v);
-  } else if constexpr (EPI == kEpiSwigluBwd) {
-    // C = dgate = dffn * W2 (layer.rs:1627-1641); SiLU-gate backward
-    // (layer.rs:1660-1666): dh3 = dg * silu(h1); dh1 = dg * h3 * sig * (1 + h1 (1 - sig)).
-    float h1[32], h3[32], dh1[32], dh3[32];
-    unpack_bf16x32(&a.u[0], h1);
-    unpack_bf16x32(&a.u[4], h3);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float sig;
-      const float sl = silu_sigmoid(h1[i], sig);
-      const float deriv = sig * (1.f + h1[i] * (1.f - sig));
-      dh3[i] = v[i] * sl;
-      dh1[i] = v[i] * h3[i] * deriv;
-    }
-    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo;
-    store_bf16x32(o + n, dh1);
-    store_bf16x32(o + p.n_half + n, dh3);
   }
 }
 
-// Epilogue of this warp's share of one 128 x BN accumulator tile: accumulator
-// row m, 32-column chunks [c0, c1).  `pre` holds chunk c0's auxiliary inputs.
+// One 32 x 32 chunk of the epilogue in the coalesced layout: w[i] holds the fp32
+// accumulators of row mbase + crow(i), columns n + ccol .. n + ccol + 3.
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const KParams& p, int mbase, int n, int lane, float4 (&w)[8],
+                                               const AuxRegs& a) {
+  const int col = n + ccol(lane);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = mbase + crow(i, lane);
+    if (m >= p.M) continue;
+    const int64_t mr = m;
+    float4 v = w[i];
+    if constexpr (EPI == kEpiBf16) {
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + mr * p.ldo + col) = pack_bf16x4(v);
+    } else if constexpr (EPI == kEpiF32 || EPI == kEpiF32Acc || EPI == kEpiResidual) {
+      if constexpr (EPI == kEpiF32Acc) {
+        if (p.beta) {
+          const float4 o = *reinterpret_cast<const float4*>(&a.u[i]);
+          v.x += o.x;
+          v.y += o.y;
+          v.z += o.z;
+          v.w += o.w;
+        }
+      }
+      if constexpr (EPI == kEpiResidual) {
+        const float4 o = *reinterpret_cast<const float4*>(&a.u[i]);
+        v.x = o.x + p.alpha * v.x;
+        v.y = o.y + p.alpha * v.y;
+        v.z = o.z + p.alpha * v.z;
+        v.w = o.w + p.alpha * v.w;
+      }
+      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + mr * p.ldo + col) = v;
+    } else if constexpr (EPI == kEpiRope) {
+      // Interleaved-pair rotation per head of 128 (kernels/sdpa_fwd.rs:18-33, 100-128):
+      //   y[2i] = x[2i] cos - x[2i+1] sin,  y[2i+1] = x[2i+1] cos + x[2i] sin
+      if (col < p.rope_cols) {
+        const float c0 = __uint_as_float(a.u[i].x), c1 = __uint_as_float(a.u[i].y);
+        const float s0 = __uint_as_float(a.u[i].z), s1 = __uint_as_float(a.u[i].w);
+        const float x0 = v.x, x1 = v.y, x2 = v.z, x3 = v.w;
+        v.x = x0 * c0 - x1 * s0;
+        v.y = x1 * c0 + x0 * s0;
+        v.z = x2 * c1 - x3 * s1;
+        v.w = x3 * c1 + x2 * s1;
+      }
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + mr * p.ldo + col) = pack_bf16x4(v);
+    } else if constexpr (EPI == kEpiSwigluBwd) {
+      // C = dgate = dffn * W2 (layer.rs:1627-1641); SiLU-gate backward
+      // (layer.rs:1660-1666): dh3 = dg * silu(h1); dh1 = dg * h3 * sig * (1 + h1 (1 - sig)).
+      const float4 h1 = unpack_bf16x4(a.u[i].x, a.u[i].y);
+      const float4 h3 = unpack_bf16x4(a.u[i].z, a.u[i].w);
+      const float hv1[4] = {h1.x, h1.y, h1.z, h1.w}, hv3[4] = {h3.x, h3.y, h3.z, h3.w};
+      const float dg[4] = {v.x, v.y, v.z, v.w};
+      float d1[4], d3[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float sig;
+        const float sl = silu_sigmoid(hv1[e], sig);
+        d3[e] = dg[e] * sl;
+        d1[e] = dg[e] * hv3[e] * (sig * (1.f + hv1[e] * (1.f - sig)));
+      }
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + mr * p.ldo;
+      *reinterpret_cast<uint2*>(o + col) = pack_bf16x4(make_float4(d1[0], d1[1], d1[2], d1[3]));
+      *reinterpret_cast<uint2*>(o + p.n_half + col) = pack_bf16x4(make_float4(d3[0], d3[1], d3[2], d3[3]));
+    }
+  }
+}
+
+// Epilogue of this warp's share of one accumulator tile: TMEM lanes of rows
+// mbase .. mbase + 31 (tbase addresses them), 32-column chunks [c0, c1) of
+// output tile column tn.  `pre` holds chunk c0's auxiliary inputs; wbuf is the
+// warp's shared-memory transpose buffer.
 template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, int m, int tn, int c0, int c1,
-                                              AuxRegs& pre) {
-  const bool row_ok = m < p.M;
-  const int64_t mrow = static_cast<int64_t>(m);
+__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, uint32_t wbuf, int lane, int mbase,
+                                              int tn, int c0, int c1, AuxRegs& pre) {
   if constexpr (EPI == kEpiSwiglu) {
     // Columns [0, BN/2) hold h1 = x W1, [BN/2, BN) hold h3 = x W3 for the
     // same BN/2 hidden units (kernels/ffn_fused.rs:46-63 semantics).
     constexpr int HALF = BN / 2;
 #pragma unroll 1
     for (int c = c0; c < c1; ++c) {
-      uint32_t g[32], u[32];
-      tmem_ld32(tbase + c * 32, g);
-      tmem_ld32(tbase + HALF + c * 32, u);
-      tmem_ld_wait();
+      float4 g[8], u[8];
+      tmem_chunk_coalesced(tbase + c * 32, wbuf, lane, g);
+      tmem_chunk_coalesced(tbase + HALF + c * 32, wbuf, lane, u);
       const int j = tn * HALF + c * 32;
-      if (row_ok && j < p.N) {
-        float h1[32], h3[32], gate[32];
+      if (j >= p.N) continue;
+      const int col = j + ccol(lane);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          h1[i] = __uint_as_float(g[i]);
-          h3[i] = __uint_as_float(u[i]);
+      for (int i = 0; i < 8; ++i) {
+        const int m = mbase + crow(i, lane);
+        if (m >= p.M) continue;
+        const int64_t mr = m;
+        const float a1[4] = {g[i].x, g[i].y, g[i].z, g[i].w}, a3[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+        float gt[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
           float sig;
-          gate[i] = silu_sigmoid(h1[i], sig) * h3[i];
+          gt[e] = silu_sigmoid(a1[e], sig) * a3[e];
         }
-        __nv_bfloat16* h13 = static_cast<__nv_bfloat16*>(p.out) + mrow * p.ldo;
-        store_bf16x32(h13 + j, h1);
-        store_bf16x32(h13 + p.n_half + j, h3);
-        store_bf16x32(static_cast<__nv_bfloat16*>(p.out2) + mrow * p.ldo2 + j, gate);
+        __nv_bfloat16* h13 = static_cast<__nv_bfloat16*>(p.out) + mr * p.ldo;
+        *reinterpret_cast<uint2*>(h13 + col) = pack_bf16x4(g[i]);
+        *reinterpret_cast<uint2*>(h13 + p.n_half + col) = pack_bf16x4(u[i]);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out2) + mr * p.ldo2 + col) =
+            pack_bf16x4(make_float4(gt[0], gt[1], gt[2], gt[3]));
       }
     }
   } else {
@@ -265,16 +283,10 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, 
     for (int c = c0; c < c1; ++c) {
       const int n = tn * BN + c * 32;
       AuxRegs nxt;
-      if (c + 1 < c1) load_aux<EPI>(p, mrow, n + 32, row_ok && n + 32 < p.N, nxt);
-      uint32_t r[32];
-      tmem_ld32(tbase + c * 32, r);
-      tmem_ld_wait();
-      if (row_ok && n < p.N) {
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        epilogue_chunk<EPI>(p, mrow, n, v, cur);
-      }
+      if (c + 1 < c1) load_aux<EPI>(p, mbase, n + 32, lane, nxt);
+      float4 w[8];
+      tmem_chunk_coalesced(tbase + c * 32, wbuf, lane, w);
+      if (n < p.N) epilogue_chunk<EPI>(p, mbase, n, lane, w, cur);
       cur = nxt;
     }
   }
@@ -287,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty_bar = full_bar + C::STAGES;
   uint64_t* tfull_bar = empty_bar + C::STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -429,17 +441,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 4) >> 2;     // which half of the tile's 32-column chunks
     constexpr int NCH = (EPI == kEpiSwiglu) ? (BN / 2) / 32 : BN / 32;
     const int c0 = half * NCH / 2, c1 = (half + 1) * NCH / 2;
+    const uint32_t wbuf = smem_u32(smem + C::EPI_OFF + (warp - 4) * kEpiBufBytes);
     int local = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (local >> 1) & 1;
       int tm, tn;
       tile_coords(tile, p.num_m, p.num_n, kRasterGroup, tm, tn);
-      const int m = tm * BM + q * 32 + lane;
+      const int mbase = tm * BM + q * 32;
       AuxRegs pre;  // first chunk's auxiliary inputs do not depend on the MMA: fetch before waiting
       if constexpr (EPI != kEpiSwiglu) {
-        const int n0 = tn * BN + c0 * 32;
-        if (c0 < c1) load_aux<EPI>(p, static_cast<int64_t>(m), n0, m < p.M && n0 < p.N, pre);
+        if (c0 < c1) load_aux<EPI>(p, mbase, tn * BN + c0 * 32, lane, pre);
       }
       bool ok = mbar_wait(&tfull_bar[acc], acc_par);
       ok = __all_sync(0xffffffffu, ok);
@@ -454,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE) + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(p, tbase, m, tn, c0, c1, pre);
+      epilogue_tile<BN, EPI>(p, tbase, wbuf, lane, mbase, tn, c0, c1, pre);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -485,7 +497,9 @@ struct Gemm2Cfg {
   static constexpr int STAGES = (BN == 256) ? 6 : 8;
   static constexpr int ACC_STRIDE = BN;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * 32 * 128;
+  static constexpr int SMEM_BYTES = BAR_OFF + 1024 + 256;
 };
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
@@ -495,7 +509,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   using C = Gemm2Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty_bar = full_bar + C::STAGES;
   uint64_t* tfull_bar = empty_bar + C::STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -648,6 +662,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int half = (warp - 4) >> 2;
     constexpr int NCH = (EPI == kEpiSwiglu) ? (BN / 2) / 32 : BN / 32;
     const int c0 = half * NCH / 2, c1 = (half + 1) * NCH / 2;
+    const uint32_t wbuf = smem_u32(smem + C::EPI_OFF + (warp - 4) * kEpiBufBytes);
     const uint32_t tempty0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);  // the leader's barriers
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
@@ -655,11 +670,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t acc_par = (local >> 1) & 1;
       int tm, tn;
       tile_coords(tile, num_m2, p.num_n, kRasterGroup / 2, tm, tn);
-      const int m = tm * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      const int mbase = tm * 256 + static_cast<int>(rank) * 128 + q * 32;
       AuxRegs pre;
       if constexpr (EPI != kEpiSwiglu) {
-        const int n0 = tn * BN + c0 * 32;
-        if (c0 < c1) load_aux<EPI>(p, static_cast<int64_t>(m), n0, m < p.M && n0 < p.N, pre);
+        if (c0 < c1) load_aux<EPI>(p, mbase, tn * BN + c0 * 32, lane, pre);
       }
       bool ok = mbar_wait(&tfull_bar[acc], acc_par);
       ok = __all_sync(0xffffffffu, ok);
@@ -674,7 +688,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE) + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(p, tbase, m, tn, c0, c1, pre);
+      epilogue_tile<BN, EPI>(p, tbase, wbuf, lane, mbase, tn, c0, c1, pre);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + 8 * acc);
