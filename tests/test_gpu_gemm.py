@@ -67,7 +67,7 @@ PAIR = [-256, -128]
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
 @pytest.mark.parametrize("bn", [128, 192, 256] + PAIR)
 def test_gemm_majors_f32(a_mn, b_mn, bn):
-    M, N, K = 256, 512, 448
+    M, N, K = 256, 512, 640  # K > stages x stage depth: the shared-memory ring wraps
     A, B, ref = operands(M, N, K, a_mn, b_mn)
     out = torch.empty(M, N, device="cuda")
     gemm(A, a_mn, B, b_mn, M, N, K, _lib.EPI_F32, out, force_bn=bn)
@@ -89,7 +89,7 @@ def test_gemm_persistent_many_tiles(bn):
 def test_gemm_ragged_edges(bn, M):
     # M not a multiple of the tile height and N not a multiple of the tile width;
     # rows past M must stay untouched
-    N, K = 352, 192
+    N, K = 352, 256
     A, B, ref = operands(M, N, K, False, False, seed=2)
     out = torch.full((M + 8, N), 7.0, device="cuda")
     gemm(A, False, B, False, M, N, K, _lib.EPI_F32, out, force_bn=bn)
@@ -182,3 +182,18 @@ def test_gemm_swiglu_bwd(bn):
     dh1 = dg * h3 * sig * (1 + h1 * (1 - sig))
     assert _rel(dh13[:, :H], dh1) < 8e-3
     assert _rel(dh13[:, H:], dh3) < 8e-3
+
+
+def test_gemm_pair_needs_two_kblock_depth():
+    # the CTA-pair kernel's stages are two 64-deep k-blocks: K % 128 != 0 is
+    # rejected when forced and routed to the single-CTA kernel when automatic
+    M, N, K = 512, 1024, 448
+    A, B, ref = operands(M, N, K, False, True, seed=9)
+    out = torch.empty(M, N, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = _lib.lib().rt_kernel_gemm(A.data_ptr(), K, 0, B.data_ptr(), N, 1, M, N, K, _lib.EPI_F32, out.data_ptr(), N,
+                                   None, 0, None, 0, 1.0, 0, None, None, 0, 0, 0, -256, err.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream)
+    assert rc != 0
+    gemm(A, False, B, True, M, N, K, _lib.EPI_F32, out)
+    assert _rel(out, ref) < TOL
