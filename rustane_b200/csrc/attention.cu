@@ -143,8 +143,10 @@ __global__ void __launch_bounds__(FWD_NT, 2)
   uint8_t* sV = sK + 2 * FWD_BN * ROW_BYTES;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int qb = gridDim.x - 1 - blockIdx.x;  // heaviest query blocks first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // grid (heads, batch, query blocks): blocks are dispatched x fastest, so the
+  // heaviest (last) query blocks of every sequence and head go out first
+  const int qb = gridDim.z - 1 - blockIdx.z;
+  const int h = blockIdx.x, b = blockIdx.y;
   const int q0 = qb * FWD_BM;
   const int64_t tok0 = static_cast<int64_t>(b) * S;
   const __nv_bfloat16* gQ = qkv + (tok0 + q0) * ldq + h * HD;
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(BWD_NT, 2)
   float* sD = sL + 2 * BWD_B;                                          // [2][64]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;  // block 0 has the most work
+  const int kb = blockIdx.z, h = blockIdx.x, b = blockIdx.y;  // key block 0 has the most work: dispatched first
   const int kv0 = kb * BWD_B;
   const int64_t tok0 = static_cast<int64_t>(b) * S;
   const int64_t stat0 = (static_cast<int64_t>(b) * nh + h) * S;
@@ -465,8 +467,8 @@ __global__ void __launch_bounds__(BWD_NT, 2)
   uint8_t* sV = sK + 2 * BWD_B * ROW_BYTES;  // [2]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int qb = gridDim.x - 1 - blockIdx.x;  // heaviest first
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int qb = gridDim.z - 1 - blockIdx.z;  // heaviest first, over all heads and sequences
+  const int h = blockIdx.x, b = blockIdx.y;
   const int q0 = qb * BWD_B;
   const int64_t tok0 = static_cast<int64_t>(b) * S;
   const int64_t stat0 = (static_cast<int64_t>(b) * nh + h) * S;
@@ -577,7 +579,7 @@ int attn_forward(const AttnArgs& a, cudaStream_t s) {
   }
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid(a.S / FWD_BM, a.heads, a.batch);
+  dim3 grid(a.heads, a.batch, a.S / FWD_BM);
   attn_fwd_kernel<<<grid, FWD_NT, FWD_SMEM, s>>>(a.qkv, a.ldq, a.D, a.out, a.ldo, a.lse2, a.S, a.heads, scale_log2);
   return cudaGetLastError();
 }
@@ -595,7 +597,7 @@ int attn_backward(const AttnArgs& a, cudaStream_t s) {
   const int M = a.batch * a.S;
   const int warps = M * a.heads;
   attn_bwd_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>(a.out, a.ldo, a.dout, a.lddo, a.dvec, M, a.S, a.heads);
-  dim3 grid(a.S / BWD_B, a.heads, a.batch);
+  dim3 grid(a.heads, a.batch, a.S / BWD_B);
   attn_bwd_dkdv_kernel<<<grid, BWD_NT, BWD_SMEM, s>>>(a.qkv, a.ldq, a.D, a.dout, a.lddo, a.lse2, a.dvec, a.dqkv,
                                                       a.lddq, a.S, a.heads, scale, scale_log2, a.rope_cos_b,
                                                       a.rope_sin_b);
