@@ -497,19 +497,22 @@ struct Gemm2Cfg {
   // commits per eight MMAs instead of four: measured 10-15% faster).
   static constexpr int SUB_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = 2 * SUB_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 3 : 4;
-  static constexpr int ACC_STRIDE = BN;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = (BN == 128) ? 4 : 3;
+  static constexpr int ACC_STRIDE = (BN == 192) ? 256 : BN;  // TMEM columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_STRIDE;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * 32 * 128;
   static constexpr int SMEM_BYTES = BAR_OFF + 1024 + 256;
 };
 
+// BN = 192 puts 96 B columns in each CTA: fine for K-major B (96 rows), not
+// for MN-major B, whose 128-byte swizzle atoms are 64 columns wide.
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const KParams p) {
   using C = Gemm2Cfg<BN>;
+  static_assert(!(B_MN && BN == 192), "MN-major B needs 64-column halves");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
@@ -772,6 +775,21 @@ int launch_inst2(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp
   X(true, true, kEpiF32Acc) X(true, true, kEpiF32) X(true, true, kEpiBf16)                   \
   X(true, false, kEpiF32) X(true, false, kEpiF32Acc)
 
+// Combinations with K-major B (the only ones the 192-wide CTA pair supports).
+#define RT_GEMM_COMBOS_BK(X)                                                                 \
+  X(false, false, kEpiBf16) X(false, false, kEpiF32) X(false, false, kEpiF32Acc)             \
+  X(false, false, kEpiResidual) X(false, false, kEpiRope) X(false, false, kEpiSwigluBwd)     \
+  X(true, false, kEpiF32) X(true, false, kEpiF32Acc)
+
+int dispatch2_192(const GemmArgs& g, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+                  cudaStream_t s) {
+#define RT_GEMM_CASE(AMN, BMN, EPI) \
+  if (g.a_mn == AMN && g.b_mn == BMN && g.epi == EPI) return launch_inst2<192, AMN, BMN, EPI>(ta, tb, kp, grid, s);
+  RT_GEMM_COMBOS_BK(RT_GEMM_CASE)
+#undef RT_GEMM_CASE
+  return -1;
+}
+
 template <int BN>
 int dispatch2(const GemmArgs& g, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
               cudaStream_t s) {
@@ -813,6 +831,7 @@ int gemm_launch_pair(const GemmArgs& g, int bn, cudaStream_t stream) {
   const bool swiglu = g.epi == kEpiSwiglu;
   if (swiglu && g.N % (bn / 2) != 0) return -1;
   if (g.K % (2 * BK) != 0) return -1;  // stages are two k-blocks deep
+  if (bn == 192 && (g.b_mn || swiglu)) return -1;
   KParams kp{};
   kp.M = g.M;
   kp.N = g.N;
@@ -852,6 +871,7 @@ int gemm_launch_pair(const GemmArgs& g, int bn, cudaStream_t stream) {
   const int max_pairs = num_sms() / 2;
   const int grid = 2 * (kp.num_tiles < max_pairs ? kp.num_tiles : max_pairs);
   if (bn == 256) return dispatch2<256>(g, ta, tb, kp, grid, stream);
+  if (bn == 192) return dispatch2_192(g, ta, tb, kp, grid, stream);
   return dispatch2<128>(g, ta, tb, kp, grid, stream);
 }
 
@@ -875,7 +895,8 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   };
   // force_bn: 128/192/256 pick the single-CTA kernel with that tile width,
   // -256/-128 the CTA-pair kernel (256-row tiles); anything else chooses.
-  if (g.force_bn == -256 || g.force_bn == -128) return gemm_launch_pair(g, -g.force_bn, stream);
+  if (g.force_bn == -256 || g.force_bn == -192 || g.force_bn == -128)
+    return gemm_launch_pair(g, -g.force_bn, stream);
   int bn = g.force_bn;
   if (bn != 128 && bn != 192 && bn != 256) {
     // time ~ waves x tile width / efficiency: 128-wide tiles are closer to the
@@ -893,11 +914,19 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
         bn = cand;
       }
     }
-    if ((!swiglu || g.N % 128 == 0) && g.K % (2 * BK) == 0) {
+    if (!g.shared_sms && (!swiglu || g.N % 128 == 0) && g.K % (2 * BK) == 0) {
       const int pairs = sms / 2;
-      const int t2 = ((g.M + 255) / 256) * (swiglu ? g.N / 128 : (g.N + 255) / 256);
-      const double cost2 = double((t2 + pairs - 1) / pairs) * 256 / 1.04;
-      if (cost2 < best * 0.999) return gemm_launch_pair(g, 256, stream);
+      int pbn = 0;
+      for (int cand : {256, 192}) {
+        if (cand == 192 && (g.b_mn || swiglu)) continue;
+        const int t2 = ((g.M + 255) / 256) * (swiglu ? g.N / (cand / 2) : (g.N + cand - 1) / cand);
+        const double cost2 = double((t2 + pairs - 1) / pairs) * cand / (cand == 256 ? 1.12 : 1.07);
+        if (cost2 < best * 0.999) {
+          best = cost2;
+          pbn = cand;
+        }
+      }
+      if (pbn) return gemm_launch_pair(g, pbn, stream);
     }
   }
   if (swiglu && (bn == 192 || g.N % (bn / 2) != 0)) bn = 128;

@@ -43,7 +43,11 @@ struct GemmArgs {
   int rope_cols = 0;
   int n_half = 0;  // kEpiSwiglu / kEpiSwigluBwd: column offset of the h3 / dh3 half
   int* err = nullptr;
-  int force_bn = 0;  // 0: choose from the wave count; 128/192/256 force a 1-CTA tile width, -256/-128 the CTA-pair kernel
+  int force_bn = 0;  // 0: choose from the wave count; 128/192/256 force a 1-CTA tile width, -256/-192/-128 the CTA-pair kernel
+  // Another GEMM may run on the SMs at the same time (a second stream): choose
+  // among the single-CTA kernels only.  Persistent CTA-pair grids lose more to
+  // SMs held by the other kernel (measured in the overlapped backward).
+  bool shared_sms = false;
 };
 
 // Returns a cudaError_t-compatible code (0 = launched) or -1 on bad arguments.

@@ -62,12 +62,19 @@ def _no_tf32():
 
 
 PAIR = [-256, -128]
+PAIR192 = -192  # 96 B rows per CTA: K-major B only
+
+
+def _skip_pair192(bn, b_mn):
+    if bn == PAIR192 and b_mn:
+        pytest.skip("the 192-wide CTA pair takes K-major B only")
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
-@pytest.mark.parametrize("bn", [128, 192, 256] + PAIR)
+@pytest.mark.parametrize("bn", [128, 192, 256] + PAIR + [PAIR192])
 def test_gemm_majors_f32(a_mn, b_mn, bn):
-    M, N, K = 256, 512, 640  # K > stages x stage depth: the shared-memory ring wraps
+    _skip_pair192(bn, b_mn)
+    M, N, K = 256, 576, 640  # K > stages x stage depth: the shared-memory ring wraps; N ragged for 192 / 256
     A, B, ref = operands(M, N, K, a_mn, b_mn)
     out = torch.empty(M, N, device="cuda")
     gemm(A, a_mn, B, b_mn, M, N, K, _lib.EPI_F32, out, force_bn=bn)
@@ -84,7 +91,7 @@ def test_gemm_persistent_many_tiles(bn):
     assert _rel(out, ref) < TOL
 
 
-@pytest.mark.parametrize("bn", [0] + PAIR)
+@pytest.mark.parametrize("bn", [0] + PAIR + [PAIR192])
 @pytest.mark.parametrize("M", [200, 328])
 def test_gemm_ragged_edges(bn, M):
     # M not a multiple of the tile height and N not a multiple of the tile width;
@@ -118,9 +125,10 @@ def test_gemm_f32_accumulate(beta, bn):
     assert _rel(out, expect) < TOL
 
 
-@pytest.mark.parametrize("bn", [0] + PAIR)
+@pytest.mark.parametrize("bn", [0] + PAIR + [PAIR192])
 @pytest.mark.parametrize("b_mn", [True, False])
 def test_gemm_residual(b_mn, bn):
+    _skip_pair192(bn, b_mn)
     M, N, K = 512, 768, 768
     A, B, ref = operands(M, N, K, False, b_mn, seed=5)
     resid = torch.randn(M, N, device="cuda")
@@ -197,3 +205,18 @@ def test_gemm_pair_needs_two_kblock_depth():
     assert rc != 0
     gemm(A, False, B, True, M, N, K, _lib.EPI_F32, out)
     assert _rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("epi", [_lib.EPI_BF16, _lib.EPI_F32])
+def test_gemm_pair192_many_tiles(epi):
+    # the backward data-gradient shape (N = D = 1536, K-major weights) on 192-wide pair tiles
+    M, N, K = 4096, 1536, 1536
+    A, B, ref = operands(M, N, K, False, False, seed=16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16 if epi == _lib.EPI_BF16 else torch.float32)
+    gemm(A, False, B, False, M, N, K, epi, out, force_bn=PAIR192)
+    assert _rel(out, ref) < (8e-3 if epi == _lib.EPI_BF16 else TOL)
+    At, Bt, reft = operands(M, N, K, True, False, seed=17)
+    acc = torch.randn(M, N, device="cuda")
+    base = acc.clone()
+    gemm(At, True, Bt, False, M, N, K, _lib.EPI_F32_ACC, acc, beta=1, force_bn=PAIR192)
+    assert _rel(acc, reft + base) < TOL
