@@ -146,26 +146,167 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// dgamma column partials: part[chunk][d] = sum over rows of the chunk (ascending)
-// of dy[m,d] * x[m,d] * rms_inv[m]; a warp reads 32 consecutive columns of a row.
-constexpr int kDgRows = 64;
+// RMSNorm backward writes one dgamma partial row per CTA of a fixed grid of
+// G = min(ceil(M / 4), kNormCtas) CTAs; dgamma_reduce adds the G rows in order.
+constexpr int kNormCtas = 148;
+constexpr int kGroupRows = 4;
+__host__ __device__ inline int norm_ctas(int M) {
+  const int g = (M + kGroupRows - 1) / kGroupRows;
+  return g < kNormCtas ? g : kNormCtas;
+}
+
+// Fallback dgamma column partials (widths the pipelined kernel does not take):
+// part[b][d] = sum over rows [b * rpb, (b + 1) * rpb) ascending of dy * x * rms_inv.
 __global__ void __launch_bounds__(256)
     rmsnorm_dgamma_part_kernel(const float* __restrict__ dy, const float* __restrict__ x,
-                               const float* __restrict__ rms_inv, float* __restrict__ part, int M, int D) {
-  __shared__ float rs[kDgRows];
+                               const float* __restrict__ rms_inv, float* __restrict__ part, int M, int D, int rpb) {
   const int d = blockIdx.x * 256 + threadIdx.x;
-  const int m0 = blockIdx.y * kDgRows;
-  const int m1 = min(M, m0 + kDgRows);
-  if (threadIdx.x < kDgRows && m0 + threadIdx.x < M) rs[threadIdx.x] = rms_inv[m0 + threadIdx.x];
-  __syncthreads();
   if (d >= D) return;
+  const int m0 = blockIdx.y * rpb;
+  const int m1 = min(M, m0 + rpb);
   float acc = 0.f;
-#pragma unroll 8
+#pragma unroll 4
   for (int m = m0; m < m1; ++m) {
     const int64_t i = static_cast<int64_t>(m) * D + d;
-    acc += dy[i] * (x[i] * rs[m - m0]);
+    acc += dy[i] * (x[i] * rms_inv[m]);
   }
   part[static_cast<int64_t>(blockIdx.y) * D + d] = acc;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// RMSNorm backward, pipelined, for D = 256 * NV2: persistent CTAs take groups
+// of 4 rows (g = blockIdx.x, + gridDim.x, ...); the dy and x rows of the next
+// STAGES - 1 groups stream into shared memory with cp.async while the current
+// group is computed, so HBM stays busy without holding rows in registers (the
+// residual-gradient row is loaded into registers at the start of its group).  Warps 2r and 2r+1 own the two halves of row r of a group.  Each
+// thread sums dgamma for its columns over the rows it handles (its CTA's groups
+// in order); the CTA adds its four row slots in order into partial row
+// blockIdx.x: deterministic.
+template <int NV2, int STAGES>
+__global__ void __launch_bounds__(256, 1)
+    rmsnorm_bwd_pipe_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                            const float* __restrict__ gamma, const float* __restrict__ rms_inv,
+                            const float* __restrict__ resid, float* __restrict__ dx,
+                            __nv_bfloat16* __restrict__ dx_bf16, float bf16_scale, float* __restrict__ part, int M,
+                            int D) {
+  extern __shared__ float4 sm[];  // [STAGES][2 arrays][kGroupRows][D / 4]
+  __shared__ float dots[8];
+  constexpr int D4 = 64 * NV2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = warp >> 1, h = warp & 1;
+  const int ngroups = (M + kGroupRows - 1) / kGroupRows;
+  const uint32_t sbase = smem_u32(sm);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+
+  auto issue = [&](int grp, int stage) {
+    if (grp < ngroups) {
+      for (int a = 0; a < 2; ++a) {
+        const float* src = a == 0 ? dy : x;
+        for (int i = threadIdx.x; i < kGroupRows * D4; i += 256) {
+          const int row = grp * kGroupRows + i / D4;
+          if (row < M)
+            cp_async16(sbase + static_cast<uint32_t>(((stage * 2 + a) * kGroupRows * D4 + i) * 16),
+                       src + static_cast<int64_t>(row) * D + (i % D4) * 4);
+        }
+      }
+    }
+    cp_async_commit();  // empty groups too: keeps the wait_group count uniform
+  };
+
+  float4 dg[NV2];
+#pragma unroll
+  for (int k = 0; k < NV2; ++k) dg[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int st = 0; st < STAGES - 1; ++st) issue(blockIdx.x + st * gridDim.x, st);
+  const float inv_d = 1.0f / static_cast<float>(D);
+  int it = 0;
+  for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
+    issue(g + (STAGES - 1) * gridDim.x, (it + STAGES - 1) % STAGES);
+    cp_async_wait<STAGES - 1>();
+    __syncthreads();  // every thread's copies of group g have landed
+    const int stage = it % STAGES;
+    const int row = g * kGroupRows + r;
+    const float4* sdy = sm + (stage * 2 + 0) * kGroupRows * D4 + r * D4;
+    const float4* sx = sm + (stage * 2 + 1) * kGroupRows * D4 + r * D4;
+    const float rinv = row < M ? rms_inv[row] : 0.f;
+    float4 q[NV2];  // residual gradient of this thread's columns, in flight during the dot product
+    if (resid && row < M) {
+      const float4* rs = reinterpret_cast<const float4*>(resid + static_cast<int64_t>(row) * D);
+#pragma unroll
+      for (int k = 0; k < NV2; ++k) q[k] = rs[h * (D4 / 2) + lane + 32 * k];
+    }
+    if (row < M) {
+      float dot = 0.f;
+#pragma unroll
+      for (int k = 0; k < NV2; ++k) {
+        const int c = h * (D4 / 2) + lane + 32 * k;
+        const float4 a = sdy[c], b = sx[c], gm = __ldg(g4 + c);
+        const float hx = b.x * rinv, hy = b.y * rinv, hz = b.z * rinv, hw = b.w * rinv;
+        dot += a.x * gm.x * hx + a.y * gm.y * hy + a.z * gm.z * hz + a.w * gm.w * hw;
+        dg[k].x += a.x * hx;  // dgamma = sum_m dy * xhat   (cpu/rmsnorm.rs:218-227)
+        dg[k].y += a.y * hy;
+        dg[k].z += a.z * hz;
+        dg[k].w += a.w * hw;
+      }
+      dot = warp_sum(dot);
+      if (lane == 0) dots[warp] = dot;
+    }
+    __syncthreads();
+    if (row < M) {
+      const float dot = (dots[2 * r] + dots[2 * r + 1]) * inv_d;
+      const int64_t off = static_cast<int64_t>(row) * D;
+      float4* o = reinterpret_cast<float4*>(dx + off);
+      uint2* ob = dx_bf16 ? reinterpret_cast<uint2*>(dx_bf16 + off) : nullptr;
+#pragma unroll
+      for (int k = 0; k < NV2; ++k) {
+        const int c = h * (D4 / 2) + lane + 32 * k;
+        const float4 a = sdy[c], b = sx[c], gm = __ldg(g4 + c);
+        float4 v;  // dx = rms_inv * (dy*gamma - xhat * dot)   (cpu/rmsnorm.rs:229-236)
+        v.x = rinv * (a.x * gm.x - (b.x * rinv) * dot);
+        v.y = rinv * (a.y * gm.y - (b.y * rinv) * dot);
+        v.z = rinv * (a.z * gm.z - (b.z * rinv) * dot);
+        v.w = rinv * (a.w * gm.w - (b.w * rinv) * dot);
+        if (resid) {
+          v.x += q[k].x;
+          v.y += q[k].y;
+          v.z += q[k].z;
+          v.w += q[k].w;
+        }
+        o[c] = v;
+        if (ob)
+          ob[c] = make_uint2(pack_bf16x2(v.x * bf16_scale, v.y * bf16_scale),
+                             pack_bf16x2(v.z * bf16_scale, v.w * bf16_scale));
+      }
+    }
+    __syncthreads();  // stage and dots free for reuse
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  float4* red = sm;  // [kGroupRows][D4]: this CTA's dgamma per row slot
+#pragma unroll
+  for (int k = 0; k < NV2; ++k) red[r * D4 + h * (D4 / 2) + lane + 32 * k] = dg[k];
+  __syncthreads();
+  float4* prow = reinterpret_cast<float4*>(part + static_cast<int64_t>(blockIdx.x) * D);
+  for (int c = threadIdx.x; c < D4; c += 256) {
+    float4 t = red[c];
+#pragma unroll
+    for (int q = 1; q < kGroupRows; ++q) {
+      const float4 u = red[q * D4 + c];
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
+    }
+    prow[c] = t;
+  }
 }
 
 // dgamma[d] = (accumulate ? dgamma[d] : 0) + sum_b part[b][d]: 32 columns per block,
@@ -505,14 +646,40 @@ int rmsnorm_fwd(const float* x, const float* gamma, __nv_bfloat16* out, float* r
   rmsnorm_fwd_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, gamma, out, rms_inv, M, D);
   return cudaGetLastError();
 }
-int rmsnorm_bwd_blocks(int M) { return (M + kDgRows - 1) / kDgRows; }
+int rmsnorm_bwd_blocks(int M) { return norm_ctas(M); }
+
+template <int NV2, int STAGES>
+int launch_norm_pipe(const float* dy, const float* x, const float* gamma, const float* rms_inv, const float* resid,
+                     float* dx, __nv_bfloat16* dx_bf16, float bf16_scale, float* part, int M, int D, cudaStream_t s) {
+  constexpr int smem = STAGES * 2 * kGroupRows * 64 * NV2 * 16;
+  static const cudaError_t attr =
+      cudaFuncSetAttribute(rmsnorm_bwd_pipe_kernel<NV2, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (attr != cudaSuccess) return attr;
+  rmsnorm_bwd_pipe_kernel<NV2, STAGES><<<norm_ctas(M), 256, smem, s>>>(dy, x, gamma, rms_inv, resid, dx, dx_bf16,
+                                                                       bf16_scale, part, M, D);
+  return cudaGetLastError();
+}
+
 int rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float* rms_inv, const float* resid,
                 float* dx, __nv_bfloat16* dx_bf16, float bf16_scale, float* dgamma_part, int M, int D,
                 cudaStream_t s) {
   if (D % 4) return -1;
-  // dgamma partials first: they read dy and x, which dx may alias
-  dim3 g2((D + 255) / 256, rmsnorm_bwd_blocks(M));
-  rmsnorm_dgamma_part_kernel<<<g2, 256, 0, s>>>(dy, x, rms_inv, dgamma_part, M, D);
+  switch (D % 256 == 0 ? D / 256 : 0) {  // shared-memory stages of 32 D bytes: 4 up to D = 1536, then 3
+    case 1: return launch_norm_pipe<1, 4>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    case 2: return launch_norm_pipe<2, 4>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    case 3: return launch_norm_pipe<3, 4>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    case 4: return launch_norm_pipe<4, 4>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    case 5: return launch_norm_pipe<5, 4>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    case 6: return launch_norm_pipe<6, 4>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    case 7: return launch_norm_pipe<7, 3>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    case 8: return launch_norm_pipe<8, 3>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale, dgamma_part, M, D, s);
+    default: break;
+  }
+  // other widths: dgamma partials first (they read dy and x, which dx may alias), then the rows
+  const int nb = norm_ctas(M);
+  const int rpb = (M + nb - 1) / nb;
+  dim3 g2((D + 255) / 256, nb);
+  rmsnorm_dgamma_part_kernel<<<g2, 256, 0, s>>>(dy, x, rms_inv, dgamma_part, M, D, rpb);
   rmsnorm_bwd_rows_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(dy, x, gamma, rms_inv, resid, dx, dx_bf16, bf16_scale,
                                                                M, D);
   return cudaGetLastError();

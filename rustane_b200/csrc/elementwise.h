@@ -20,8 +20,8 @@ int embed_scatter(const float* dx, const int32_t* perm, const int32_t* seg_start
 int rmsnorm_fwd(const float* x, const float* gamma, __nv_bfloat16* out, float* rms_inv, int M, int D, cudaStream_t s);
 
 // dx = rms_inv * (dy*gamma - xhat * mean(dy*gamma*xhat)) + resid (resid may be null);
-// dx_bf16 (optional) = bf16(bf16_scale * dx); per-block dgamma partials [nblk][D].
-// Returns the number of partial rows written (to pass to dgamma_reduce).
+// dx_bf16 (optional) = bf16(bf16_scale * dx); dgamma partials [rmsnorm_bwd_blocks(M)][D]
+// (fixed row partition and order) for dgamma_reduce.
 int rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float* rms_inv, const float* resid,
                 float* dx, __nv_bfloat16* dx_bf16, float bf16_scale, float* dgamma_part, int M, int D,
                 cudaStream_t s);
