@@ -14,8 +14,9 @@
 // h*128, D + h*128, 2D + h*128; O [M, D]; dqkv [M, 3D] (same column layout).
 // The softmax statistic is kept in the log2 domain: lse2 = max + log2(sum).
 //
-// The matrix products use mma.sync m16n8k16 (bf16 -> fp32) fed by ldmatrix
-// from 128-byte-swizzled shared-memory tiles filled with cp.async.
+// The backward's matrix products use mma.sync m16n8k16 (bf16 -> fp32) fed by
+// ldmatrix from 128-byte-swizzled shared-memory tiles filled with cp.async; the
+// forward runs on tcgen05 / TMEM (attention_tc.cu).
 #include "attention.h"
 #include "common.cuh"
 
@@ -127,164 +128,6 @@ __device__ __forceinline__ void rope_bwd_frag(float (&acc)[16][4], int pos_a, in
     acc[nt][2] = cb * e0 + sb * e1;
     acc[nt][3] = -sb * e0 + cb * e1;
   }
-}
-
-// ----------------------------------------------------------------- forward
-// grid (S/128, heads, batch), 256 threads: warp w owns query rows q0 + 16w .. +15.
-constexpr int FWD_BM = 128, FWD_BN = 64, FWD_NT = 256;
-constexpr int FWD_SMEM = (FWD_BM + 4 * FWD_BN) * ROW_BYTES;  // Q + 2x(K, V)
-
-__global__ void __launch_bounds__(FWD_NT, 2)
-    attn_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int D, __nv_bfloat16* __restrict__ O,
-                    int64_t ldo, float* __restrict__ lse2, int S, int nh, float scale_log2) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + FWD_BM * ROW_BYTES;
-  uint8_t* sV = sK + 2 * FWD_BN * ROW_BYTES;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
-  // grid (heads, batch, query blocks): blocks are dispatched x fastest, so the
-  // heaviest (last) query blocks of every sequence and head go out first
-  const int qb = gridDim.z - 1 - blockIdx.z;
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int q0 = qb * FWD_BM;
-  const int64_t tok0 = static_cast<int64_t>(b) * S;
-  const __nv_bfloat16* gQ = qkv + (tok0 + q0) * ldq + h * HD;
-  const __nv_bfloat16* gK = qkv + tok0 * ldq + D + h * HD;
-  const __nv_bfloat16* gV = qkv + tok0 * ldq + 2 * D + h * HD;
-
-  load_tile<FWD_BM, FWD_NT>(sQ, gQ, ldq, tid);
-  load_tile<FWD_BN, FWD_NT>(sK, gK, ldq, tid);
-  load_tile<FWD_BN, FWD_NT>(sV, gV, ldq, tid);
-  cp_async_commit();
-
-  const int nkb = (q0 + FWD_BM) / FWD_BN;
-  const int r0 = warp * 16;
-  const int qa = q0 + r0 + g, qbr = qa + 8;  // query positions of this thread's rows
-  float acc[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  const uint32_t sQa = smem_u32(sQ);
-
-  for (int j = 0; j < nkb; ++j) {
-    if (j + 1 < nkb) {
-      const int nb = (j + 1) & 1;
-      load_tile<FWD_BN, FWD_NT>(sK + nb * FWD_BN * ROW_BYTES, gK + static_cast<int64_t>(j + 1) * FWD_BN * ldq, ldq,
-                                tid);
-      load_tile<FWD_BN, FWD_NT>(sV + nb * FWD_BN * ROW_BYTES, gV + static_cast<int64_t>(j + 1) * FWD_BN * ldq, ldq,
-                                tid);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const int key0 = j * FWD_BN;
-    if (key0 <= q0 + r0 + 15) {  // this warp has at least one unmasked key in the block
-      const uint32_t kt = smem_u32(sK + (j & 1) * FWD_BN * ROW_BYTES);
-      const uint32_t vt = smem_u32(sV + (j & 1) * FWD_BN * ROW_BYTES);
-      float s[8][4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        uint32_t a[4];
-        lds_a(a, sQa, r0, kk, lane);
-#pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          uint32_t bb[4];
-          lds_b_nk(bb, kt, np * 16, kk, lane);
-          mma16816(s[2 * np], a, bb[0], bb[1]);
-          mma16816(s[2 * np + 1], a, bb[2], bb[3]);
-        }
-      }
-      // scale, mask, online softmax
-      const bool diag = key0 + FWD_BN - 1 > q0 + r0;
-      float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = key0 + nt * 8 + 2 * t + e;
-          float xa = s[nt][e] * scale_log2, xb = s[nt][2 + e] * scale_log2;
-          if (diag) {
-            if (key > qa) xa = -INFINITY;
-            if (key > qbr) xb = -INFINITY;
-          }
-          s[nt][e] = xa;
-          s[nt][2 + e] = xb;
-          mx_a = fmaxf(mx_a, xa);
-          mx_b = fmaxf(mx_b, xb);
-        }
-      }
-#pragma unroll
-      for (int o = 1; o <= 2; o <<= 1) {
-        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
-        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
-      }
-      const float nm_a = fmaxf(m_a, mx_a), nm_b = fmaxf(m_b, mx_b);
-      const float base_a = nm_a == -INFINITY ? 0.f : nm_a, base_b = nm_b == -INFINITY ? 0.f : nm_b;
-      const float corr_a = exp2f(m_a - base_a), corr_b = exp2f(m_b - base_b);
-      m_a = nm_a;
-      m_b = nm_b;
-      float rs_a = 0.f, rs_b = 0.f;
-      uint32_t pa[8][2];
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float p0 = exp2f(s[nt][0] - base_a), p1 = exp2f(s[nt][1] - base_a);
-        const float p2 = exp2f(s[nt][2] - base_b), p3 = exp2f(s[nt][3] - base_b);
-        rs_a += p0 + p1;
-        rs_b += p2 + p3;
-        pa[nt][0] = pack_bf16x2(p0, p1);
-        pa[nt][1] = pack_bf16x2(p2, p3);
-      }
-      l_a = l_a * corr_a + rs_a;
-      l_b = l_b * corr_b + rs_b;
-#pragma unroll
-      for (int nt = 0; nt < 16; ++nt) {
-        acc[nt][0] *= corr_a;
-        acc[nt][1] *= corr_a;
-        acc[nt][2] *= corr_b;
-        acc[nt][3] *= corr_b;
-      }
-      // O += P V
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint32_t a[4] = {pa[2 * kk][0], pa[2 * kk][1], pa[2 * kk + 1][0], pa[2 * kk + 1][1]};
-#pragma unroll
-        for (int np = 0; np < 8; ++np) {
-          uint32_t bb[4];
-          lds_b_kn(bb, vt, kk * 16, np, lane);
-          mma16816(acc[2 * np], a, bb[0], bb[1]);
-          mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
-        }
-      }
-    }
-    __syncthreads();
-  }
-  // finalize
-#pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, o);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, o);
-  }
-  const float inv_a = 1.f / l_a, inv_b = 1.f / l_b;
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    acc[nt][0] *= inv_a;
-    acc[nt][1] *= inv_a;
-    acc[nt][2] *= inv_b;
-    acc[nt][3] *= inv_b;
-  }
-  if (t == 0) {
-    float* L = lse2 + (static_cast<int64_t>(b) * nh + h) * S;
-    L[qa] = m_a + __log2f(l_a);
-    L[qbr] = m_b + __log2f(l_b);
-  }
-  frag_to_tile(sQ, r0, acc, lane);
-  __syncthreads();
-  store_tile<FWD_BM, FWD_NT>(sQ, O + (tok0 + q0) * ldo + h * HD, ldo, tid);
 }
 
 // ------------------------------------------------------ backward: prepare
@@ -569,25 +412,9 @@ bool g_attr_done = false;
 
 }  // namespace
 
-int attn_forward(const AttnArgs& a, cudaStream_t s) {
-  if (a.S % 128 != 0 || a.hd != HD || a.D != a.heads * HD) return -1;
-  if (!g_attr_done) {
-    cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM);
-    cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
-    g_attr_done = true;
-  }
-  const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid(a.heads, a.batch, a.S / FWD_BM);
-  attn_fwd_kernel<<<grid, FWD_NT, FWD_SMEM, s>>>(a.qkv, a.ldq, a.D, a.out, a.ldo, a.lse2, a.S, a.heads, scale_log2);
-  return cudaGetLastError();
-}
-
 int attn_backward(const AttnArgs& a, cudaStream_t s) {
   if (a.S % 128 != 0 || a.hd != HD || a.D != a.heads * HD) return -1;
   if (!g_attr_done) {
-    cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM);
     cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
     cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
     g_attr_done = true;

@@ -22,8 +22,10 @@ struct AttnArgs {
   int64_t lddq = 0;
   const float* rope_cos_b = nullptr;  // [hd/2][S]
   const float* rope_sin_b = nullptr;
+  int* err = nullptr;  // device error word (bounded-wait timeouts of the tcgen05 kernel)
 };
 
+// Forward on tcgen05 / TMEM (attention_tc.cu).
 int attn_forward(const AttnArgs& a, cudaStream_t s);
 int attn_backward(const AttnArgs& a, cudaStream_t s);
 

@@ -877,6 +877,11 @@ int gemm_launch_pair(const GemmArgs& g, int bn, cudaStream_t stream) {
 
 }  // namespace
 
+bool make_tmap_bf16(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                    uint32_t box_inner, uint32_t box_outer) {
+  return encoder_ready() && make_tmap(tm, ptr, inner, outer, ld, box_inner, box_outer);
+}
+
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (!encoder_ready()) return -2;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.K % BK != 0 || g.N % 32 != 0) return -1;

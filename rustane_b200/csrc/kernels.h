@@ -2,6 +2,7 @@
 // All pointers are device pointers; every launch is asynchronous on `stream`.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -52,6 +53,10 @@ struct GemmArgs {
 
 // Returns a cudaError_t-compatible code (0 = launched) or -1 on bad arguments.
 int gemm_launch(const GemmArgs& g, cudaStream_t stream);
+// 2-D bf16 tensor map [outer][inner] (row stride ld elements), 128-byte swizzled
+// boxes of box_inner x box_outer; false if the driver entry point is missing.
+bool make_tmap_bf16(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                    uint32_t box_inner, uint32_t box_outer);
 int num_sms();
 
 }  // namespace rt

@@ -490,7 +490,7 @@ int layer_forward(rt_ctx* c, int l, const rt::LayerActs& A, const float* x_in, f
   {  // causal attention (sdpa_fwd.rs:130-150)
     rt::AttnArgs a;
     a.batch = batch; a.S = S; a.heads = c->heads_loc; a.hd = cfg.hd; a.D = Dl;
-    a.qkv = A.qkv; a.ldq = 3 * Dl; a.out = A.attn; a.ldo = Dl; a.lse2 = A.lse2;
+    a.qkv = A.qkv; a.ldq = 3 * Dl; a.out = A.attn; a.ldo = Dl; a.lse2 = A.lse2; a.err = c->d_err;
     const double fl = 4.0 * batch * c->heads_loc * double(S) * S / 2.0 * cfg.hd;
     RT_LAUNCH(launch(c, 1, fl, 1, [&] { return rt::attn_forward(a, c->stream); }), "attention fwd");
   }
@@ -710,7 +710,7 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
       a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
       a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
       a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv[p]; a.lddq = 3 * D;
-      a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b;
+      a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b; a.err = c->d_err;
       const double fl = 2.5 * 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
       RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward(a, ms); }), "attention bwd");
     }

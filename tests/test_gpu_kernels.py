@@ -187,11 +187,14 @@ def _attn_ref(qkv, B, S, H):
     return o.permute(0, 2, 1, 3).reshape(B * S, D), lse
 
 
-@pytest.mark.parametrize("B,S,H", [(2, 256, 2), (1, 512, 3)])
-def test_attention_forward(B, S, H):
+# amp = 6 makes the row max grow by more than 2^8 between key blocks, which the
+# tcgen05 forward handles by rescaling the TMEM accumulator
+@pytest.mark.parametrize("amp", [1.0, 6.0])
+@pytest.mark.parametrize("B,S,H", [(2, 256, 2), (1, 512, 3), (3, 384, 1)])
+def test_attention_forward(B, S, H, amp):
     D = H * 128
     g = torch.Generator(device="cuda").manual_seed(5)
-    qkv = torch.randn(B * S, 3 * D, generator=g, device="cuda").bfloat16()
+    qkv = (amp * torch.randn(B * S, 3 * D, generator=g, device="cuda")).bfloat16()
     out = torch.empty(B * S, D, device="cuda", dtype=torch.bfloat16)
     lse2 = torch.empty(B, H, S, device="cuda")
     ok(L.rt_kernel_attention_fwd(qkv.data_ptr(), out.data_ptr(), lse2.data_ptr(), B, S, H, stream()))
