@@ -104,6 +104,11 @@ typedef struct rt_timings {
   int64_t kernel_launches; /* every kernel this context launched since creation */
 } rt_timings;
 
+/* crates/engine/src/cpu/adam.rs:12-30 (AdamConfig) for the single-layer step. */
+typedef struct rt_adam_config {
+  float lr, beta1, beta2, eps, weight_decay;
+} rt_adam_config;
+
 typedef struct rt_ctx rt_ctx;
 
 /* --------------------------------------------------------- context / data */
@@ -185,6 +190,26 @@ RT_API int rt_sync(rt_ctx* ctx, float* loss_out);
 RT_API int rt_ctx_stream(const rt_ctx* ctx, void** stream_out);
 /* Bytes the last host-token call copied host -> device. */
 RT_API int rt_last_h2d_bytes(const rt_ctx* ctx, int64_t* out);
+
+/* ------------------------------------------------------- single layer
+ * One transformer layer of a training context on its own (the engine's layer
+ * API and the Phase-3 training loop).  Activations use the reference layout:
+ * per sequence channel-first [dim][seq] fp32, `batch` sequences back to back.
+ * The layer's weights are layer `layer` of the context's weights. */
+
+/* layer::forward (layer.rs:443-...): y = the layer output; keeps the layer's
+ * activations for rt_layer_backward (and invalidates the last model forward). */
+RT_API int rt_layer_forward(rt_ctx* ctx, int layer, const float* x, int batch, float* y);
+/* layer::backward (layer.rs:1355-1858) of the last rt_layer_forward of `layer`:
+ * dx = gradient at the layer input; the layer's weight gradients accumulate
+ * into the device grads (LayerGrads semantics). */
+RT_API int rt_layer_backward(rt_ctx* ctx, int layer, const float* dy, float* dx);
+/* training::train_step (training.rs:61-97): forward, loss = mean(y^2) (MSE
+ * against zero), the layer's gradients zeroed then dy = 2 y / n backward,
+ * and training::update_weights (training.rs:41-59): AdamW (adam::step,
+ * cpu/adam.rs:37-85) with one config for all nine tensors, t 1-based. */
+RT_API int rt_layer_train_step(rt_ctx* ctx, int layer, const float* x, int batch, uint32_t t,
+                               const rt_adam_config* cfg, float* loss_out);
 
 /* ------------------------------------------------------- multi-GPU */
 

@@ -774,6 +774,69 @@ OR_API void or_grads_zero(const OrConfig* cfg, OrModel* g) {
 }
 
 // One optimizer step over `batch` explicit sequences, equivalent to
+// ------------------------------------------------------- single layer
+// layer::forward / layer::backward of one sequence (layer.rs:443-..., 1355-...):
+// x, x_next, dy, dx in the reference's channel-first [D][S] layout.  The forward
+// cache lives in the first cache slot of ws and is what the next backward reads.
+OR_API void or_layer_forward(const OrConfig* cfg, OrWs* ws, const OrLayer* w, const float* x, float* x_next) {
+  layer_forward(*cfg, *ws, *w, x, ws->seqs[0].caches[0], x_next);
+}
+// Accumulates into g (LayerGrads semantics).
+OR_API void or_layer_backward(const OrConfig* cfg, OrWs* ws, const OrLayer* w, const float* dy, OrLayer* g,
+                              float* dx) {
+  layer_backward(*cfg, *ws, *w, ws->seqs[0].caches[0], dy, *g, dx);
+}
+
+namespace {
+template <class F>
+void for_each_layer_tensor(const OrConfig& c, OrLayer* l, F&& f) {
+  const int64_t D = c.dim, Q = c.q_dim, KV = c.kv_dim, H = c.hidden;
+  f(l->wq, D * Q);
+  f(l->wk, D * KV);
+  f(l->wv, D * KV);
+  f(l->wo, Q * D);
+  f(l->w1, D * H);
+  f(l->w3, D * H);
+  f(l->w2, D * H);
+  f(l->gamma1, D);
+  f(l->gamma2, D);
+}
+}  // namespace
+
+// training::train_step (training.rs:61-97): forward, loss = mean(x_next^2) (an MSE
+// against zero, summed in f32 order), dy = 2 x_next / n, grads zeroed, backward,
+// then training::update_weights (training.rs:41-59): adam::step on each tensor
+// with one AdamConfig (no lr groups, no clipping).  Returns the loss.
+OR_API float or_layer_train_step(const OrConfig* cfg, OrWs* ws, OrLayer* w, OrLayer* g, OrLayer* m, OrLayer* v,
+                                 const float* x, uint32_t t, float lr, float beta1, float beta2, float eps,
+                                 float weight_decay) {
+  const int64_t n = int64_t(cfg->dim) * cfg->seq;
+  std::vector<float> y(n), dy(n), dx(n);
+  or_layer_forward(cfg, ws, w, x, y.data());
+  float loss = 0.f;
+  for (int64_t i = 0; i < n; ++i) loss += y[i] * y[i];
+  loss /= static_cast<float>(n);
+  const float scale = 2.0f / static_cast<float>(n);
+  for (int64_t i = 0; i < n; ++i) dy[i] = y[i] * scale;
+  for_each_layer_tensor(*cfg, g, [](float* p, int64_t k) { std::fill(p, p + k, 0.f); });
+  or_layer_backward(cfg, ws, w, dy.data(), g, dx.data());
+  float* wp[9];
+  float* gp[9];
+  float* mp[9];
+  float* vp[9];
+  int64_t np[9];
+  int i = 0;
+  for_each_layer_tensor(*cfg, w, [&](float* p, int64_t k) { wp[i] = p; np[i++] = k; });
+  i = 0;
+  for_each_layer_tensor(*cfg, g, [&](float* p, int64_t) { gp[i++] = p; });
+  i = 0;
+  for_each_layer_tensor(*cfg, m, [&](float* p, int64_t) { mp[i++] = p; });
+  i = 0;
+  for_each_layer_tensor(*cfg, v, [&](float* p, int64_t) { vp[i++] = p; });
+  for (int k = 0; k < 9; ++k) or_adam_step(wp[k], gp[k], mp[k], vp[k], np[k], t, lr, beta1, beta2, eps, weight_decay);
+  return loss;
+}
+
 // full_model::train_step (full_model.rs:661-714) with accum_steps = batch:
 // zero grads, forward+backward per sequence, clip decision, lr, AdamW(t = step+1).
 OR_API float or_train_step_batch(const OrConfig* cfg, OrModel* w, OrModel* g, OrModel* m, OrModel* v,

@@ -14,7 +14,7 @@ from pathlib import Path
 import numpy as np
 
 from rustane_b200.model import ModelConfig, RtModelConfig
-from rustane_b200.tensors import ModelOptState, ModelTensors, RtModelPtrs
+from rustane_b200.tensors import LayerTensors, ModelOptState, ModelTensors, RtLayerPtrs, RtModelPtrs
 
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "_build" / "liboracle.so"
@@ -109,6 +109,15 @@ def lib(threads: int | None = None) -> ctypes.CDLL:
                                                      ctypes.c_void_p, F]),
             "or_train_positions": (None, [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int64, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_int64)]),
+            "or_layer_forward": (None, [ctypes.POINTER(RtModelConfig), ctypes.c_void_p, ctypes.POINTER(RtLayerPtrs),
+                                        F, F]),
+            "or_layer_backward": (None, [ctypes.POINTER(RtModelConfig), ctypes.c_void_p,
+                                         ctypes.POINTER(RtLayerPtrs), F, ctypes.POINTER(RtLayerPtrs), F]),
+            "or_layer_train_step": (ctypes.c_float, [ctypes.POINTER(RtModelConfig), ctypes.c_void_p,
+                                                     ctypes.POINTER(RtLayerPtrs), ctypes.POINTER(RtLayerPtrs),
+                                                     ctypes.POINTER(RtLayerPtrs), ctypes.POINTER(RtLayerPtrs), F,
+                                                     ctypes.c_uint32, ctypes.c_float, ctypes.c_float,
+                                                     ctypes.c_float, ctypes.c_float, ctypes.c_float]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(h, name)
@@ -230,6 +239,27 @@ class Oracle:
                                           ctypes.byref(mp), ctypes.byref(vp), up(tokens), up(targets), n, step,
                                           ctypes.byref(tc), self.ws, ctypes.byref(raw))
         return loss, raw.value
+
+
+    # ---- single layer (layer::forward / layer::backward / training::train_step), x in [D][S]
+    def layer_forward(self, lw: LayerTensors, x: np.ndarray) -> np.ndarray:
+        y = np.empty_like(x)
+        wp = lw.c_ptrs()
+        self.L.or_layer_forward(ctypes.byref(self.c_cfg), self.ws, ctypes.byref(wp), fp(x), fp(y))
+        return y
+
+    def layer_backward(self, lw: LayerTensors, dy: np.ndarray, g: LayerTensors) -> np.ndarray:
+        dx = np.empty_like(dy)
+        wp, gp = lw.c_ptrs(), g.c_ptrs()
+        self.L.or_layer_backward(ctypes.byref(self.c_cfg), self.ws, ctypes.byref(wp), fp(dy), ctypes.byref(gp), fp(dx))
+        return dx
+
+    def layer_train_step(self, lw: LayerTensors, g: LayerTensors, m: LayerTensors, v: LayerTensors,
+                         x: np.ndarray, t: int, lr: float, beta1: float = 0.9, beta2: float = 0.999,
+                         eps: float = 1e-8, weight_decay: float = 0.01) -> float:
+        ptrs = [a.c_ptrs() for a in (lw, g, m, v)]
+        return self.L.or_layer_train_step(ctypes.byref(self.c_cfg), self.ws, *[ctypes.byref(p) for p in ptrs], fp(x),
+                                          t, lr, beta1, beta2, eps, weight_decay)
 
 
 def learning_rate(step: int, tc: OrTrainConfig) -> float:

@@ -35,6 +35,10 @@ class RtTrainConfig(ctypes.Structure):
                 ("accum_steps", ctypes.c_uint32), ("grad_clip", ctypes.c_float), ("softcap", ctypes.c_float)]
 
 
+class RtAdamConfig(ctypes.Structure):  # crates/engine/src/cpu/adam.rs:12-30
+    _fields_ = [(n, ctypes.c_float) for n in ("lr", "beta1", "beta2", "eps", "weight_decay")]
+
+
 class RtTimings(ctypes.Structure):
     _fields_ = [(n, ctypes.c_double) for n in ("fwd_ms", "bwd_ms", "comm_ms", "opt_ms", "gemm_ms", "gemm_flops",
                                                "attn_ms", "attn_flops", "other_ms")] + \
@@ -82,6 +86,10 @@ SIGNATURES: dict[str, tuple] = {
     "rt_nccl_unique_id": (c_int, [c_uint8_p]),
     "rt_dist_init": (c_int, [c_void_p, c_int, c_int, c_uint8_p, c_int, c_int]),
     "rt_grad_allreduce": (c_int, [c_void_p]),
+    "rt_layer_forward": (c_int, [c_void_p, c_int, c_float_p, c_int, c_float_p]),
+    "rt_layer_backward": (c_int, [c_void_p, c_int, c_float_p, c_float_p]),
+    "rt_layer_train_step": (c_int, [c_void_p, c_int, c_float_p, c_int, c_uint32, ctypes.POINTER(RtAdamConfig),
+                                    c_float_p]),
     "rt_profile": (c_int, [c_void_p, c_int]),
     "rt_get_timings": (c_int, [c_void_p, ctypes.POINTER(RtTimings)]),
     "rt_kernel_gemm": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int,

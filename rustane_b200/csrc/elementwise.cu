@@ -519,11 +519,13 @@ __global__ void __launch_bounds__(256) adam_kernel(float* __restrict__ param, co
 }
 
 // ---------------------------------------------------------------- misc
-__global__ void cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n4) {
+__global__ void cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n4,
+                                 float scale) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const float4 v = reinterpret_cast<const float4*>(src)[i];
-    reinterpret_cast<uint2*>(dst)[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    reinterpret_cast<uint2*>(dst)[i] =
+        make_uint2(pack_bf16x2(v.x * scale, v.y * scale), pack_bf16x2(v.z * scale, v.w * scale));
   }
 }
 __global__ void fill_kernel(float* __restrict__ dst, int64_t n, float value) {
@@ -731,8 +733,11 @@ int adam_step(const AdamArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 int cast_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s) {
+  return cast_bf16_scaled(src, dst, n, 1.0f, s);
+}
+int cast_bf16_scaled(const float* src, __nv_bfloat16* dst, int64_t n, float scale, cudaStream_t s) {
   if (n % 4) return -1;
-  cast_bf16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(src, dst, n / 4);
+  cast_bf16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(src, dst, n / 4, scale);
   return cudaGetLastError();
 }
 int fill_f32(float* dst, int64_t n, float value, cudaStream_t s) {

@@ -79,6 +79,8 @@ int init_normal_block(float* dst, int64_t rows, int64_t cols, int64_t dst_ld, in
 
 // Elementwise helpers.
 int cast_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s);
+// dst = bf16(scale * src)
+int cast_bf16_scaled(const float* src, __nv_bfloat16* dst, int64_t n, float scale, cudaStream_t s);
 int fill_f32(float* dst, int64_t n, float value, cudaStream_t s);
 // Counter-based N(0, std) init: element i of a stream with the given seed.
 int init_normal(float* dst, int64_t n, uint64_t seed, float std, cudaStream_t s);

@@ -597,6 +597,126 @@ int allreduce_range(rt_ctx* c, int64_t begin, int64_t end, cudaStream_t st) {
 // temporaries; with overlap_allreduce each layer's gradients are all-reduced on
 // s_comm right after its weight-gradient GEMMs.  On return the main stream has
 // waited for all of it.
+// Backward of layer l (layer.rs:1606-1858): dy = gradient at the layer output
+// (fp32), dffn[l & 1] = bf16(alpha * dy); writes dy_next = gradient at the layer
+// input and, for l > 0, dffn[(l - 1) & 1] = bf16(alpha * dy_next).  Weight
+// gradients go to the arena (beta = 0 overwrites) on the weight-gradient stream,
+// whose last GEMM records ev_dw_done[l].
+int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) {
+  const auto& cfg = c->cfg;
+  const int D = cfg.dim, H = cfg.hidden, S = cfg.seq, L = cfg.nlayers;
+  const int batch = c->cur_batch, M = batch * S;
+  const float alpha = alpha_of(cfg);
+  const bf16* W = c->params_bf16;
+  const float* P = c->params;
+  float* Gr = c->grads;
+  const int nblk = rt::rmsnorm_bwd_blocks(M);
+  cudaStream_t ms = c->stream, ds = c->s_dw;
+  int rc;
+  const rt::LayerActs& A = c->acts[l];
+  const auto& o = c->layer_off[l];
+  const int p = l & 1;
+  // the parity-p temporaries were last read by the weight GEMMs of layer l + 2
+  if (l + 2 < L) cudaStreamWaitEvent(ms, c->ev_dw_done[l + 2], 0);
+  {  // ffnBwdW2t + SiLU backward (layer.rs:1627-1667)
+    rt::GemmArgs g;
+    g.a = c->dffn[p]; g.lda = D;
+    g.b = W + o.w2; g.ldb = H; g.b_mn = true;
+    g.M = M; g.N = H; g.K = D;
+    g.epi = rt::kEpiSwigluBwd; g.aux = A.h13; g.ld_aux = 2 * H; g.out = c->dh13[p]; g.ldo = 2 * H; g.n_half = H;
+    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
+    if ((rc = gemm(c, g, "dgate"))) return rc;
+  }
+  cudaEventRecord(c->ev_dgate[l], ms);
+  cudaStreamWaitEvent(ds, c->ev_dgate[l], 0);
+  {  // dW2 += dffn^T gate (layer.rs:1754)
+    rt::GemmArgs g;
+    g.a = c->dffn[p]; g.lda = D; g.a_mn = true;
+    g.b = A.gate; g.ldb = H; g.b_mn = true;
+    g.M = D; g.N = H; g.K = M;
+    g.epi = rt::kEpiF32Acc; g.out = Gr + o.w2; g.ldo = H; g.beta = beta;
+    if ((rc = gemm(c, g, "dW2", ds))) return rc;
+  }
+  {  // dW1 | dW3 += x2norm^T (dh1 | dh3) (layer.rs:1692, 1787)
+    rt::GemmArgs g;
+    g.a = A.x2n; g.lda = D; g.a_mn = true;
+    g.b = c->dh13[p]; g.ldb = 2 * H; g.b_mn = true;
+    g.M = D; g.N = 2 * H; g.K = M;
+    g.epi = rt::kEpiF32Acc; g.out = Gr + o.w13; g.ldo = 2 * H; g.beta = beta;
+    if ((rc = gemm(c, g, "dW13", ds))) return rc;
+  }
+  {  // ffnBwdW13t: dx_ffn = dh1 W1^T + dh3 W3^T (layer.rs:1671-1699)
+    rt::GemmArgs g;
+    g.a = c->dh13[p]; g.lda = 2 * H;
+    g.b = W + o.w13; g.ldb = 2 * H; g.b_mn = false;
+    g.M = M; g.N = D; g.K = 2 * H;
+    g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
+    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
+    if ((rc = gemm(c, g, "dx_ffn"))) return rc;
+  }
+  // RMSNorm2 backward + dy (layer.rs:1702-1706); dx2s = alpha * dx2
+  RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s[p], alpha, c->dgamma_part,
+                              M, D, ms),
+           "rmsnorm2 bwd");
+  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma2, D, beta, ms), "dgamma2");
+  cudaEventRecord(c->ev_rms2[l], ms);
+  cudaStreamWaitEvent(ds, c->ev_rms2[l], 0);
+  {  // dWo += attn^T dx2s (layer.rs:1753)
+    rt::GemmArgs g;
+    g.a = A.attn; g.lda = cfg.q_dim; g.a_mn = true;
+    g.b = c->dx2s[p]; g.ldb = D; g.b_mn = true;
+    g.M = cfg.q_dim; g.N = D; g.K = M;
+    g.epi = rt::kEpiF32Acc; g.out = Gr + o.wo; g.ldo = D; g.beta = beta;
+    if ((rc = gemm(c, g, "dWo", ds))) return rc;
+  }
+  {  // wotBwd: da = dx2s Wo^T (layer.rs:1709-1733)
+    rt::GemmArgs g;
+    g.a = c->dx2s[p]; g.lda = D;
+    g.b = W + o.wo; g.ldb = D; g.b_mn = false;
+    g.M = M; g.N = cfg.q_dim; g.K = D;
+    g.epi = rt::kEpiBf16; g.out = c->da; g.ldo = cfg.q_dim;
+    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
+    if ((rc = gemm(c, g, "da"))) return rc;
+  }
+  {  // sdpaBwd1 + sdpaBwd2 + RoPE backward (layer.rs:1736-1798)
+    rt::AttnArgs a;
+    a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
+    a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
+    a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv[p]; a.lddq = 3 * D;
+    a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b; a.err = c->d_err;
+    const double fl = 2.5 * 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
+    RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward(a, ms); }), "attention bwd");
+  }
+  cudaEventRecord(c->ev_attn[l], ms);
+  cudaStreamWaitEvent(ds, c->ev_attn[l], 0);
+  {  // dWq | dWk | dWv += xnorm^T (dq | dk | dv) (layer.rs:1838-1840)
+    rt::GemmArgs g;
+    g.a = A.xn; g.lda = D; g.a_mn = true;
+    g.b = c->dqkv[p]; g.ldb = 3 * D; g.b_mn = true;
+    g.M = D; g.N = 3 * D; g.K = M;
+    g.epi = rt::kEpiF32Acc; g.out = Gr + o.wqkv; g.ldo = 3 * D; g.beta = beta;
+    if ((rc = gemm(c, g, "dWqkv", ds))) return rc;
+  }
+  cudaEventRecord(c->ev_dw_done[l], ds);
+  {  // qBwd + kvBwd: dx_attn = dq Wq^T + dk Wk^T + dv Wv^T (layer.rs:1800-1850)
+    rt::GemmArgs g;
+    g.a = c->dqkv[p]; g.lda = 3 * D;
+    g.b = W + o.wqkv; g.ldb = 3 * D; g.b_mn = false;
+    g.M = M; g.N = D; g.K = 3 * D;
+    g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
+    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
+    if ((rc = gemm(c, g, "dx_attn"))) return rc;
+  }
+  // RMSNorm1 backward + dx2 (layer.rs:1853-1857); alpha * dx for the layer below, into the
+  // other parity's dffn, last read by the weight GEMMs of layer l + 1
+  if (l > 0 && l + 1 < L) cudaStreamWaitEvent(ms, c->ev_dw_done[l + 1], 0);
+  RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next,
+                              l > 0 ? c->dffn[(l - 1) & 1] : nullptr, alpha, c->dgamma_part, M, D, ms),
+           "rmsnorm1 bwd");
+  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma1, D, beta, ms), "dgamma1");
+  return RT_OK;
+}
+
 int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   const auto& cfg = c->cfg;
   const int D = cfg.dim, H = cfg.hidden, V = cfg.vocab, S = cfg.seq, L = cfg.nlayers;
@@ -640,112 +760,13 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   float* dy = c->dy_a;
   float* dy_next = c->dy_b;
   for (int l = L - 1; l >= 0; --l) {
-    const rt::LayerActs& A = c->acts[l];
+    if ((rc = layer_backward(c, l, dy, dy_next, beta))) return rc;
     const auto& o = c->layer_off[l];
-    const int p = l & 1;
-    // the parity-p temporaries were last read by the weight GEMMs of layer l + 2
-    if (l + 2 < L) cudaStreamWaitEvent(ms, c->ev_dw_done[l + 2], 0);
-    {  // ffnBwdW2t + SiLU backward (layer.rs:1627-1667)
-      rt::GemmArgs g;
-      g.a = c->dffn[p]; g.lda = D;
-      g.b = W + o.w2; g.ldb = H; g.b_mn = true;
-      g.M = M; g.N = H; g.K = D;
-      g.epi = rt::kEpiSwigluBwd; g.aux = A.h13; g.ld_aux = 2 * H; g.out = c->dh13[p]; g.ldo = 2 * H; g.n_half = H;
-      g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
-      if ((rc = gemm(c, g, "dgate"))) return rc;
-    }
-    cudaEventRecord(c->ev_dgate[l], ms);
-    cudaStreamWaitEvent(ds, c->ev_dgate[l], 0);
-    {  // dW2 += dffn^T gate (layer.rs:1754)
-      rt::GemmArgs g;
-      g.a = c->dffn[p]; g.lda = D; g.a_mn = true;
-      g.b = A.gate; g.ldb = H; g.b_mn = true;
-      g.M = D; g.N = H; g.K = M;
-      g.epi = rt::kEpiF32Acc; g.out = Gr + o.w2; g.ldo = H; g.beta = beta;
-      if ((rc = gemm(c, g, "dW2", ds))) return rc;
-    }
-    {  // dW1 | dW3 += x2norm^T (dh1 | dh3) (layer.rs:1692, 1787)
-      rt::GemmArgs g;
-      g.a = A.x2n; g.lda = D; g.a_mn = true;
-      g.b = c->dh13[p]; g.ldb = 2 * H; g.b_mn = true;
-      g.M = D; g.N = 2 * H; g.K = M;
-      g.epi = rt::kEpiF32Acc; g.out = Gr + o.w13; g.ldo = 2 * H; g.beta = beta;
-      if ((rc = gemm(c, g, "dW13", ds))) return rc;
-    }
-    {  // ffnBwdW13t: dx_ffn = dh1 W1^T + dh3 W3^T (layer.rs:1671-1699)
-      rt::GemmArgs g;
-      g.a = c->dh13[p]; g.lda = 2 * H;
-      g.b = W + o.w13; g.ldb = 2 * H; g.b_mn = false;
-      g.M = M; g.N = D; g.K = 2 * H;
-      g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
-      g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
-      if ((rc = gemm(c, g, "dx_ffn"))) return rc;
-    }
-    // RMSNorm2 backward + dy (layer.rs:1702-1706); dx2s = alpha * dx2
-    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s[p], alpha, c->dgamma_part,
-                                M, D, ms),
-             "rmsnorm2 bwd");
-    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma2, D, beta, ms), "dgamma2");
-    cudaEventRecord(c->ev_rms2[l], ms);
-    cudaStreamWaitEvent(ds, c->ev_rms2[l], 0);
-    {  // dWo += attn^T dx2s (layer.rs:1753)
-      rt::GemmArgs g;
-      g.a = A.attn; g.lda = cfg.q_dim; g.a_mn = true;
-      g.b = c->dx2s[p]; g.ldb = D; g.b_mn = true;
-      g.M = cfg.q_dim; g.N = D; g.K = M;
-      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wo; g.ldo = D; g.beta = beta;
-      if ((rc = gemm(c, g, "dWo", ds))) return rc;
-    }
-    {  // wotBwd: da = dx2s Wo^T (layer.rs:1709-1733)
-      rt::GemmArgs g;
-      g.a = c->dx2s[p]; g.lda = D;
-      g.b = W + o.wo; g.ldb = D; g.b_mn = false;
-      g.M = M; g.N = cfg.q_dim; g.K = D;
-      g.epi = rt::kEpiBf16; g.out = c->da; g.ldo = cfg.q_dim;
-      g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
-      if ((rc = gemm(c, g, "da"))) return rc;
-    }
-    {  // sdpaBwd1 + sdpaBwd2 + RoPE backward (layer.rs:1736-1798)
-      rt::AttnArgs a;
-      a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
-      a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
-      a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv[p]; a.lddq = 3 * D;
-      a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b; a.err = c->d_err;
-      const double fl = 2.5 * 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
-      RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward(a, ms); }), "attention bwd");
-    }
-    cudaEventRecord(c->ev_attn[l], ms);
-    cudaStreamWaitEvent(ds, c->ev_attn[l], 0);
-    {  // dWq | dWk | dWv += xnorm^T (dq | dk | dv) (layer.rs:1838-1840)
-      rt::GemmArgs g;
-      g.a = A.xn; g.lda = D; g.a_mn = true;
-      g.b = c->dqkv[p]; g.ldb = 3 * D; g.b_mn = true;
-      g.M = D; g.N = 3 * D; g.K = M;
-      g.epi = rt::kEpiF32Acc; g.out = Gr + o.wqkv; g.ldo = 3 * D; g.beta = beta;
-      if ((rc = gemm(c, g, "dWqkv", ds))) return rc;
-    }
-    cudaEventRecord(c->ev_dw_done[l], ds);
     if (c->overlap_allreduce) {  // this layer's matrices are final: reduce them while backward continues
       cudaStreamWaitEvent(c->s_comm, c->ev_dw_done[l], 0);
       if (l == L - 1) cudaEventRecord(c->ev[4], c->s_comm);
       if ((rc = allreduce_range(c, o.wqkv, o.w2 + int64_t(D) * H, c->s_comm))) return rc;
     }
-    {  // qBwd + kvBwd: dx_attn = dq Wq^T + dk Wk^T + dv Wv^T (layer.rs:1800-1850)
-      rt::GemmArgs g;
-      g.a = c->dqkv[p]; g.lda = 3 * D;
-      g.b = W + o.wqkv; g.ldb = 3 * D; g.b_mn = false;
-      g.M = M; g.N = D; g.K = 3 * D;
-      g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
-      g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
-      if ((rc = gemm(c, g, "dx_attn"))) return rc;
-    }
-    // RMSNorm1 backward + dx2 (layer.rs:1853-1857); alpha * dx for the layer below, into the
-    // other parity's dffn, last read by the weight GEMMs of layer l + 1
-    if (l > 0 && l + 1 < L) cudaStreamWaitEvent(ms, c->ev_dw_done[l + 1], 0);
-    RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next,
-                                l > 0 ? c->dffn[(l - 1) & 1] : nullptr, alpha, c->dgamma_part, M, D, ms),
-             "rmsnorm1 bwd");
-    RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma1, D, beta, ms), "dgamma1");
     std::swap(dy, dy_next);
   }
   // embedding scatter-add (full_model.rs:330), after the dE GEMM
@@ -1271,6 +1292,136 @@ RT_API int rt_update_weights(rt_ctx* c, uint32_t t, float lr, const rt_train_con
   cudaEventRecord(c->ev[7], c->stream);
   c->ev_recorded |= 8u;
   return wait_stream(c);
+}
+
+// ================================================================= single layer
+namespace {
+
+// [batch][D][S] (reference, channel-first) <-> [batch * S][D] (token-major)
+void cf_to_tm(const float* cf, float* tm, int batch, int D, int S) {
+  for (int b = 0; b < batch; ++b)
+    for (int d = 0; d < D; ++d)
+      for (int s = 0; s < S; ++s) tm[(int64_t(b) * S + s) * D + d] = cf[(int64_t(b) * D + d) * S + s];
+}
+void tm_to_cf(const float* tm, float* cf, int batch, int D, int S) {
+  for (int b = 0; b < batch; ++b)
+    for (int d = 0; d < D; ++d)
+      for (int s = 0; s < S; ++s) cf[(int64_t(b) * D + d) * S + s] = tm[(int64_t(b) * S + s) * D + d];
+}
+
+int check_layer(rt_ctx* c, int layer) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (layer < 0 || layer >= c->cfg.nlayers) return set_err(c, RT_ERR_ARG, "layer index out of range");
+  if (!c->weights_set) return set_err(c, RT_ERR_STATE, "weights not uploaded");
+  if (c->tp) return set_err(c, RT_ERR_STATE, "single-layer calls run on unsharded contexts");
+  return RT_OK;
+}
+
+// Forward of layer `l` on host input x (reference layout); output left in c->x_out.
+int layer_forward_host(rt_ctx* c, int l, const float* x, int batch) {
+  const int D = c->cfg.dim, S = c->cfg.seq;
+  const int64_t n = int64_t(batch) * S * D;
+  std::vector<float> h(n);
+  cf_to_tm(x, h.data(), batch, D, S);
+  const rt::LayerActs& A = c->acts[l];
+  RT_CUDA(cudaMemcpyAsync(A.x, h.data(), sizeof(float) * n, cudaMemcpyHostToDevice, c->stream), "layer input");
+  int rc;
+  if ((rc = layer_forward(c, l, A, A.x, c->x_out, batch))) return rc;
+  c->cur_batch = batch;
+  c->fwd_done = false;  // the model-level activations of layer l were overwritten
+  c->layer_fwd = l;
+  RT_CUDA(cudaStreamSynchronize(c->stream), "layer forward");  // h is read by the async copy
+  return RT_OK;
+}
+
+// Backward of layer `l` from the device gradient c->dy_a; dx into c->dy_b; both streams joined.
+int layer_backward_dev(rt_ctx* c, int l, int beta) {
+  const int64_t n = int64_t(c->cur_batch) * c->cfg.seq * c->cfg.dim;
+  RT_OTHER(1, rt::cast_bf16_scaled(c->dy_a, c->dffn[l & 1], n, alpha_of(c->cfg), c->stream), "alpha * dy");
+  int rc;
+  if ((rc = layer_backward(c, l, c->dy_a, c->dy_b, beta))) return rc;
+  cudaStreamWaitEvent(c->stream, c->ev_dw_done[l], 0);
+  return RT_OK;
+}
+
+}  // namespace
+
+RT_API int rt_layer_forward(rt_ctx* c, int layer, const float* x, int batch, float* y) {
+  int rc;
+  if ((rc = check_layer(c, layer))) return rc;
+  if (!x || !y) return set_err(c, RT_ERR_ARG, "null buffer");
+  if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
+  cudaSetDevice(c->device);
+  if ((rc = layer_forward_host(c, layer, x, batch))) return rc;
+  const int D = c->cfg.dim, S = c->cfg.seq;
+  std::vector<float> h(int64_t(batch) * S * D);
+  RT_CUDA(cudaMemcpyAsync(h.data(), c->x_out, sizeof(float) * h.size(), cudaMemcpyDeviceToHost, c->stream), "y");
+  if ((rc = wait_stream(c))) return rc;
+  tm_to_cf(h.data(), y, batch, D, S);
+  return RT_OK;
+}
+
+RT_API int rt_layer_backward(rt_ctx* c, int layer, const float* dy, float* dx) {
+  int rc;
+  if ((rc = check_layer(c, layer))) return rc;
+  if (!dy || !dx) return set_err(c, RT_ERR_ARG, "null buffer");
+  if (c->layer_fwd != layer) return set_err(c, RT_ERR_STATE, "rt_layer_backward without rt_layer_forward of the layer");
+  cudaSetDevice(c->device);
+  if ((rc = materialize_zero_grads(c))) return rc;  // accumulate semantics from here on
+  const int batch = c->cur_batch, D = c->cfg.dim, S = c->cfg.seq;
+  const int64_t n = int64_t(batch) * S * D;
+  std::vector<float> h(n);
+  cf_to_tm(dy, h.data(), batch, D, S);
+  RT_CUDA(cudaMemcpyAsync(c->dy_a, h.data(), sizeof(float) * n, cudaMemcpyHostToDevice, c->stream), "dy");
+  if ((rc = layer_backward_dev(c, layer, 1))) return rc;
+  RT_CUDA(cudaMemcpyAsync(h.data(), c->dy_b, sizeof(float) * n, cudaMemcpyDeviceToHost, c->stream), "dx");
+  if ((rc = wait_stream(c))) return rc;
+  tm_to_cf(h.data(), dx, batch, D, S);
+  return RT_OK;
+}
+
+RT_API int rt_layer_train_step(rt_ctx* c, int layer, const float* x, int batch, uint32_t t,
+                               const rt_adam_config* ac, float* loss_out) {
+  int rc;
+  if ((rc = check_layer(c, layer))) return rc;
+  if (!x || !ac || t == 0) return set_err(c, RT_ERR_ARG, "null input / config or t == 0");
+  if (batch <= 0 || batch > c->max_batch) return set_err(c, RT_ERR_SHAPE, "batch exceeds the context's max_batch");
+  cudaSetDevice(c->device);
+  if ((rc = materialize_zero_grads(c))) return rc;  // other layers keep their (zero) gradients
+  if ((rc = layer_forward_host(c, layer, x, batch))) return rc;
+  const int64_t n = int64_t(batch) * c->cfg.seq * c->cfg.dim;
+  // loss = mean(y^2) through the fixed-order L2 norm; dy = 2 y / n
+  RT_OTHER(2, rt::sumsq_norm(c->x_out, n, c->norm_partials, c->d_norm, c->stream), "layer loss");
+  RT_OTHER(1, rt::scale_f32(c->x_out, c->dy_a, n, 2.0f / static_cast<float>(n), c->stream), "dy");
+  // grads.zero_out() of this layer: its weight gradients are overwritten (beta = 0)
+  if ((rc = layer_backward_dev(c, layer, 0))) return rc;
+  const auto& o = c->layer_off[layer];
+  const int64_t D = c->cfg.dim, H = c->cfg.hidden;
+  rt::AdamArgs a;
+  a.param = c->params;
+  a.grad = c->grads;
+  a.m = c->mom1;
+  a.v = c->mom2;
+  a.param_bf16 = c->params_bf16;
+  a.nseg = 3;
+  a.seg[0] = {o.wqkv, o.w2 + D * H, ac->lr, ac->weight_decay, 1};
+  a.seg[1] = {o.gamma1, o.gamma1 + D, ac->lr, ac->weight_decay, 0};
+  a.seg[2] = {o.gamma2, o.gamma2 + D, ac->lr, ac->weight_decay, 0};
+  a.beta1 = ac->beta1;
+  a.beta2 = ac->beta2;
+  a.eps = ac->eps;
+  a.bc1 = 1.0f / (1.0f - powi_f32(ac->beta1, t));
+  a.bc2 = 1.0f / (1.0f - powi_f32(ac->beta2, t));
+  a.grad_scale = 1.0f;
+  RT_OTHER(1, rt::adam_step(a, c->stream), "layer adam");
+  float norm = 0.f;
+  RT_CUDA(cudaMemcpyAsync(&norm, c->d_norm, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss");
+  if ((rc = wait_stream(c))) return rc;
+  const float loss = norm * norm / static_cast<float>(n);
+  if (loss_out) *loss_out = loss;
+  if (!std::isfinite(loss)) return set_err(c, RT_ERR_NONFINITE, "loss is not finite");
+  return RT_OK;
 }
 
 // Everything of train_step after the batch is on the device; async unless

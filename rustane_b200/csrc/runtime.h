@@ -67,6 +67,7 @@ struct rt_ctx {
   cudaStream_t stream = nullptr;
   std::string last_error;
   int* d_err = nullptr;
+  int layer_fwd = -1;  // layer of the last rt_layer_forward (its activations are cached)
 
   // parameter arenas (elements): [embed | matrices | gammas]
   int64_t n_params = 0, n_embed = 0, n_matrix_end = 0;

@@ -210,6 +210,34 @@ class CompiledKernels:
         self._last_batch = batch
         return loss.value
 
+    # -------------------------------------------------------- single layer
+    # layer::forward / layer::backward / training::train_step on layer `layer` of
+    # the uploaded weights; x, dy, y, dx per sequence in the reference's
+    # channel-first [dim][seq] layout.
+    def layer_forward(self, layer: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        batch = x.size // (self.cfg.dim * self.cfg.seq)
+        y = np.empty_like(x)
+        self._check(lib().rt_layer_forward(self.handle, layer, _fptr(x), batch, _fptr(y)))
+        return y
+
+    def layer_backward(self, layer: int, dy: np.ndarray) -> np.ndarray:
+        dy = np.ascontiguousarray(dy, np.float32)
+        dx = np.empty_like(dy)
+        self._check(lib().rt_layer_backward(self.handle, layer, _fptr(dy), _fptr(dx)))
+        return dx
+
+    def layer_train_step(self, layer: int, x: np.ndarray, t: int, lr: float, beta1: float = 0.9,
+                         beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.01) -> float:
+        """training::train_step (training.rs:61-97); AdamConfig defaults of cpu/adam.rs:21-29."""
+        x = np.ascontiguousarray(x, np.float32)
+        batch = x.size // (self.cfg.dim * self.cfg.seq)
+        ac = _lib.RtAdamConfig(lr, beta1, beta2, eps, weight_decay)
+        loss = ctypes.c_float()
+        self._check(lib().rt_layer_train_step(self.handle, layer, _fptr(x), batch, t, ctypes.byref(ac),
+                                              ctypes.byref(loss)))
+        return loss.value
+
     # ---------------------------------------------------------- multi-GPU
     @staticmethod
     def nccl_unique_id() -> bytes:

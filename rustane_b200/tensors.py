@@ -56,6 +56,16 @@ class LayerTensors:
     def arrays(self):
         return [getattr(self, f) for f in LAYER_FIELDS]
 
+    @classmethod
+    def zeros(cls, cfg: ModelConfig) -> "LayerTensors":
+        return cls(**{n: np.zeros(shp, np.float32) for n, shp in layer_shapes(cfg).items()})
+
+    def copy(self) -> "LayerTensors":
+        return LayerTensors(*[a.copy() for a in self.arrays()])
+
+    def c_ptrs(self) -> RtLayerPtrs:
+        return RtLayerPtrs(*[_fptr(a) for a in self.arrays()])
+
 
 @dataclass
 class ModelTensors:
