@@ -247,7 +247,7 @@ RT_API int rt_get_timings(rt_ctx* ctx, rt_timings* out);
  * the cblas_sgemm calls (crates/engine/src/cpu/vdsp.rs:128-136, :287-321).
  * force_bn: 0 lets the library choose; 128/192/256 force the single-CTA kernel
  * with that output tile width; -256/-128 force the CTA-pair kernel (a cluster
- * of two SMs owns a 256 x 256 / 256 x 128 tile; K must be a multiple of 128,
+ * of two SMs owns a 256 x 256 / 256 x 192 / 256 x 128 tile; 192 needs K-major B,
  * else RT_ERR_SHAPE). */
 RT_API int rt_kernel_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int M, int N,
                           int K, int epi, void* out, int64_t ldo, void* out2, int64_t ldo2, const void* aux,

@@ -40,7 +40,12 @@ template <int BN>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // One 64-deep k-block per stage: with 48 KB per k-block at BN = 256, stages
+  // of two k-blocks leave only two stages, which measured 10-12% slower here
+  // (the CTA-pair kernel, at 32 KB per k-block and SM, does use two).
+  static constexpr int KPS = 1;  // k-blocks per stage
+  static constexpr int SUB_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = KPS * SUB_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : (BN == 192 ? 4 : 6);
   static constexpr int ACC_STRIDE = (BN == 192) ? 256 : BN;  // TMEM columns per accumulator buffer
   static constexpr int TMEM_COLS = 2 * ACC_STRIDE;
@@ -345,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int tm, tn;
         tile_coords(tile, p.num_m, p.num_n, kRasterGroup, tm, tn);
         const int m0 = tm * BM;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int kb = 0; kb < p.num_kb; kb += C::KPS, ++it) {  // one stage: k-blocks kb .. kb + KPS - 1
           const int stage = it % C::STAGES;
           const uint32_t phase = (it / C::STAGES) & 1;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
@@ -358,30 +363,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          uint8_t* sA = smem + stage * C::STAGE_BYTES;
-          uint8_t* sB = sA + C::A_BYTES;
-          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
-          const int k0 = kb * BK;
-          if constexpr (A_MN) {
+          const int nsub = min(C::KPS, p.num_kb - kb);
+          mbar_arrive_expect_tx(&full_bar[stage], nsub * C::SUB_BYTES);
+          for (int sub = 0; sub < nsub; ++sub) {
+            uint8_t* sA = smem + stage * C::STAGE_BYTES + sub * C::SUB_BYTES;
+            uint8_t* sB = sA + C::A_BYTES;
+            const int k0 = (kb + sub) * BK;
+            if constexpr (A_MN) {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sA + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
-          } else {
-            tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
-          }
-          if constexpr (B_MN) {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j) {
-              int nphys;
-              if constexpr (EPI == kEpiSwiglu) {
-                constexpr int HALF = BN / 2;
-                nphys = (j < HALF / 64) ? tn * HALF + 64 * j : p.n_half + tn * HALF + 64 * (j - HALF / 64);
-              } else {
-                nphys = tn * BN + 64 * j;
-              }
-              tma_load_2d(sB + j * 8192, &tmB, &full_bar[stage], nphys, k0);
+              for (int j = 0; j < BM / 64; ++j) tma_load_2d(sA + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+            } else {
+              tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
             }
-          } else {
-            tma_load_2d(sB, &tmB, &full_bar[stage], k0, tn * BN);
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) {
+                int nphys;
+                if constexpr (EPI == kEpiSwiglu) {
+                  constexpr int HALF = BN / 2;
+                  nphys = (j < HALF / 64) ? tn * HALF + 64 * j : p.n_half + tn * HALF + 64 * (j - HALF / 64);
+                } else {
+                  nphys = tn * BN + 64 * j;
+                }
+                tma_load_2d(sB + j * 8192, &tmB, &full_bar[stage], nphys, k0);
+              }
+            } else {
+              tma_load_2d(sB, &tmB, &full_bar[stage], k0, tn * BN);
+            }
           }
         }
       }
@@ -407,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE);
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int kb = 0; kb < p.num_kb; kb += C::KPS, ++it) {
           const int stage = it % C::STAGES;
           const uint32_t phase = (it / C::STAGES) & 1;
           if (!mbar_wait(&full_bar[stage], phase) || *abort_flag) {
@@ -417,15 +425,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + C::A_BYTES;
+          const int nsub = min(C::KPS, p.num_kb - kb);
+          for (int sub = 0; sub < nsub; ++sub) {
+            const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES + sub * C::SUB_BYTES);
+            const uint32_t b_addr = a_addr + C::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024)
-                                     : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
-                                     : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                       : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+              const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                       : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+              umma_bf16(d_tmem, ad, bd, idesc, (kb | sub | kk) != 0 ? 1u : 0u);
+            }
           }
           umma_commit(&empty_bar[stage]);  // frees the smem slot once these MMAs finish
         }
@@ -493,8 +504,8 @@ struct Gemm2Cfg {
   static constexpr int BNH = BN / 2;  // B columns held by each CTA
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = BNH * BK * 2;
-  // A stage holds two 64-deep k-blocks (one mbarrier round trip and one pair of
-  // commits per eight MMAs instead of four: measured 10-15% faster).
+  // A stage holds up to two 64-deep k-blocks (one mbarrier round trip and one
+  // pair of commits per eight MMAs instead of four: measured 10-15% faster).
   static constexpr int SUB_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = 2 * SUB_BYTES;
   static constexpr int STAGES = (BN == 128) ? 4 : 3;
@@ -569,7 +580,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int tm, tn;
         tile_coords(tile, num_m2, p.num_n, kRasterGroup / 2, tm, tn);
         const int m0 = tm * 256 + static_cast<int>(rank) * 128;
-        for (int ks = 0; ks < p.num_kb / 2; ++ks, ++it) {  // ks: stage of two k-blocks
+        for (int kb = 0; kb < p.num_kb; kb += 2, ++it) {  // one stage: k-blocks kb and kb + 1
           const int stage = it % C::STAGES;
           const uint32_t phase = (it / C::STAGES) & 1;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1) || *abort_flag) {
@@ -578,12 +589,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+          const int nsub = p.num_kb - kb > 1 ? 2 : 1;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * nsub * C::SUB_BYTES);  // both CTAs' copies
           const uint32_t fbar = full0 + 8 * stage;
-          for (int sub = 0; sub < 2; ++sub) {
+          for (int sub = 0; sub < nsub; ++sub) {
             uint8_t* sA = smem + stage * C::STAGE_BYTES + sub * C::SUB_BYTES;
             uint8_t* sB = sA + C::A_BYTES;
-            const int k0 = (2 * ks + sub) * BK;
+            const int k0 = (kb + sub) * BK;
             if constexpr (A_MN) {
 #pragma unroll
               for (int j = 0; j < 2; ++j) tma_load_2d_pair(sA + j * 8192, &tmA, fbar, m0 + 64 * j, k0);
@@ -633,7 +645,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE);
-        for (int ks = 0; ks < p.num_kb / 2; ++ks, ++it) {  // ks: stage of two k-blocks
+        for (int kb = 0; kb < p.num_kb; kb += 2, ++it) {
           const int stage = it % C::STAGES;
           const uint32_t phase = (it / C::STAGES) & 1;
           if (!mbar_wait(&full_bar[stage], phase) || *abort_flag) {
@@ -643,8 +655,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-#pragma unroll
-          for (int sub = 0; sub < 2; ++sub) {
+          const int nsub = p.num_kb - kb > 1 ? 2 : 1;
+          for (int sub = 0; sub < nsub; ++sub) {
             const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES + sub * C::SUB_BYTES);
             const uint32_t b_addr = a_addr + C::A_BYTES;
 #pragma unroll
@@ -653,7 +665,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                        : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
               const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
                                        : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-              umma_bf16_pair(d_tmem, ad, bd, idesc, (ks | kk | sub) != 0 ? 1u : 0u);
+              umma_bf16_pair(d_tmem, ad, bd, idesc, (kb | kk | sub) != 0 ? 1u : 0u);
             }
           }
           umma_commit_pair(empty0 + 8 * stage);  // both CTAs' slots are free once these finish
@@ -830,7 +842,6 @@ namespace {
 int gemm_launch_pair(const GemmArgs& g, int bn, cudaStream_t stream) {
   const bool swiglu = g.epi == kEpiSwiglu;
   if (swiglu && g.N % (bn / 2) != 0) return -1;
-  if (g.K % (2 * BK) != 0) return -1;  // stages are two k-blocks deep
   if (bn == 192 && (g.b_mn || swiglu)) return -1;
   KParams kp{};
   kp.M = g.M;
@@ -919,7 +930,7 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
         bn = cand;
       }
     }
-    if (!g.shared_sms && (!swiglu || g.N % 128 == 0) && g.K % (2 * BK) == 0) {
+    if (!g.shared_sms && (!swiglu || g.N % 128 == 0)) {
       const int pairs = sms / 2;
       int pbn = 0;
       for (int cand : {256, 192}) {

@@ -192,19 +192,18 @@ def test_gemm_swiglu_bwd(bn):
     assert _rel(dh13[:, H:], dh3) < 8e-3
 
 
-def test_gemm_pair_needs_two_kblock_depth():
-    # the CTA-pair kernel's stages are two 64-deep k-blocks: K % 128 != 0 is
-    # rejected when forced and routed to the single-CTA kernel when automatic
+def test_gemm_odd_kblock_count():
+    # stages hold two 64-deep k-blocks; an odd count ends with a half stage
     M, N, K = 512, 1024, 448
     A, B, ref = operands(M, N, K, False, True, seed=9)
+    for bn in (128, 192, 256, -256, -128):
+        out = torch.empty(M, N, device="cuda")
+        gemm(A, False, B, True, M, N, K, _lib.EPI_F32, out, force_bn=bn)
+        assert _rel(out, ref) < TOL, bn
+    A2, B2, ref2 = operands(M, N, K, True, False, seed=10)
     out = torch.empty(M, N, device="cuda")
-    err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    rc = _lib.lib().rt_kernel_gemm(A.data_ptr(), K, 0, B.data_ptr(), N, 1, M, N, K, _lib.EPI_F32, out.data_ptr(), N,
-                                   None, 0, None, 0, 1.0, 0, None, None, 0, 0, 0, -256, err.data_ptr(),
-                                   torch.cuda.current_stream().cuda_stream)
-    assert rc != 0
-    gemm(A, False, B, True, M, N, K, _lib.EPI_F32, out)
-    assert _rel(out, ref) < TOL
+    gemm(A2, True, B2, False, M, N, K, _lib.EPI_F32, out, force_bn=-192)
+    assert _rel(out, ref2) < TOL
 
 
 @pytest.mark.parametrize("epi", [_lib.EPI_BF16, _lib.EPI_F32])
