@@ -211,6 +211,39 @@ RT_API int rt_layer_backward(rt_ctx* ctx, int layer, const float* dy, float* dx)
 RT_API int rt_layer_train_step(rt_ctx* ctx, int layer, const float* x, int batch, uint32_t t,
                                const rt_adam_config* cfg, float* loss_out);
 
+/* ------------------------------------------------------- host I/O
+ * The engine's training-data and checkpoint files, host side only (no device). */
+
+/* TokenData (crates/engine/src/data.rs:11-39): a memory-mapped file of
+ * little-endian uint16 token ids. */
+typedef struct rt_tokens rt_tokens;
+RT_API int rt_tokens_open(const char* path, rt_tokens** out);
+RT_API int rt_tokens_close(rt_tokens* t);
+RT_API int rt_tokens_len(const rt_tokens* t, int64_t* n_out);
+/* Tokens [start, start + len) widened to uint32. */
+RT_API int rt_tokens_read(const rt_tokens* t, int64_t start, int64_t len, uint32_t* out);
+/* Training window of microbatch `micro` at `step` (bin/train.rs:285-290,
+ * data.rs:92-95): pos = (step*7919 + micro*104729) mod (n - seq - 1);
+ * tokens = data[pos, pos+seq), targets = data[pos+1, pos+seq+1). */
+RT_API int rt_tokens_train_window(const rt_tokens* t, uint32_t step, uint32_t micro, int seq, uint32_t* tokens,
+                                  uint32_t* targets);
+/* Validation window `vs` (bin/train.rs:128-131): pos = (vs*seq) mod (n - seq - 1). */
+RT_API int rt_tokens_val_window(const rt_tokens* t, uint32_t vs, int seq, uint32_t* tokens, uint32_t* targets);
+/* compute_bpb (data.rs:67-89) over n per-token losses (nats) and their target
+ * ids, with the token_bytes.bin table (int32 byte length per id). */
+RT_API int rt_compute_bpb(const float* losses, const uint32_t* targets, int64_t n, const int32_t* token_bytes,
+                          int32_t n_token_bytes, float* bpb_out, float* nats_out, int64_t* bytes_out);
+/* RSTK checkpoint (save_checkpoint, bin/train.rs:165-202): version 1 (m = v =
+ * NULL) is the reference's file byte for byte; version 2 appends the AdamW
+ * moments m and v, which the reference does not save.  The reader takes
+ * either version, checks dim / nlayers / vocab / seq against cfg, and fills m
+ * and v when the file has them and they are given. */
+RT_API int rt_checkpoint_write(const char* path, const rt_model_config* cfg, uint32_t step, const rt_model_ptrs* w,
+                               const rt_model_ptrs* m, const rt_model_ptrs* v);
+RT_API int rt_checkpoint_read(const char* path, const rt_model_config* cfg, uint32_t* step_out,
+                              uint32_t* version_out, const rt_model_ptrs* w, const rt_model_ptrs* m,
+                              const rt_model_ptrs* v);
+
 /* ------------------------------------------------------- multi-GPU */
 
 /* NCCL unique id (128 bytes) for rank 0 to broadcast to the other ranks. */

@@ -8,9 +8,10 @@ is the host-side mirror of the reference engine crate's API:
     loss = full_model.forward(cfg, kernels, weights, tokens, targets, 0.0)
 """
 from . import engine as full_model
+from ._lib import RustaneError
 from .engine import CompiledKernels, TrainConfig, learning_rate, random_weights
 from .model import ModelConfig
 from .tensors import ModelGrads, ModelOptState, ModelTensors, ModelWeights
 
 __all__ = ["ModelConfig", "ModelWeights", "ModelGrads", "ModelOptState", "ModelTensors", "TrainConfig",
-           "CompiledKernels", "full_model", "learning_rate", "random_weights"]
+           "CompiledKernels", "full_model", "learning_rate", "random_weights", "RustaneError"]

@@ -86,6 +86,19 @@ SIGNATURES: dict[str, tuple] = {
     "rt_nccl_unique_id": (c_int, [c_uint8_p]),
     "rt_dist_init": (c_int, [c_void_p, c_int, c_int, c_uint8_p, c_int, c_int]),
     "rt_grad_allreduce": (c_int, [c_void_p]),
+    "rt_tokens_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_void_p)]),
+    "rt_tokens_close": (c_int, [c_void_p]),
+    "rt_tokens_len": (c_int, [c_void_p, ctypes.POINTER(c_int64)]),
+    "rt_tokens_read": (c_int, [c_void_p, c_int64, c_int64, c_uint32_p]),
+    "rt_tokens_train_window": (c_int, [c_void_p, c_uint32, c_uint32, c_int, c_uint32_p, c_uint32_p]),
+    "rt_tokens_val_window": (c_int, [c_void_p, c_uint32, c_int, c_uint32_p, c_uint32_p]),
+    "rt_compute_bpb": (c_int, [c_float_p, c_uint32_p, c_int64, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32,
+                               c_float_p, c_float_p, ctypes.POINTER(c_int64)]),
+    "rt_checkpoint_write": (c_int, [ctypes.c_char_p, P_CFG, c_uint32, ctypes.POINTER(RtModelPtrs),
+                                    ctypes.POINTER(RtModelPtrs), ctypes.POINTER(RtModelPtrs)]),
+    "rt_checkpoint_read": (c_int, [ctypes.c_char_p, P_CFG, ctypes.POINTER(c_uint32), ctypes.POINTER(c_uint32),
+                                   ctypes.POINTER(RtModelPtrs), ctypes.POINTER(RtModelPtrs),
+                                   ctypes.POINTER(RtModelPtrs)]),
     "rt_layer_forward": (c_int, [c_void_p, c_int, c_float_p, c_int, c_float_p]),
     "rt_layer_backward": (c_int, [c_void_p, c_int, c_float_p, c_float_p]),
     "rt_layer_train_step": (c_int, [c_void_p, c_int, c_float_p, c_int, c_uint32, ctypes.POINTER(RtAdamConfig),
