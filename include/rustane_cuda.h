@@ -300,6 +300,17 @@ RT_API int rt_kernel_attention_bwd(const void* qkv, const void* out, const float
                                    float* dvec, void* dqkv, const float* rope_cos_b, const float* rope_sin_b,
                                    int batch, int seq, int heads, void* stream);
 
+/* The same backward on the tcgen05 tensor cores (what the model step runs):
+ * dK / dV per 128-key block with S^T, dP^T, dV, dK in TMEM, then dQ from the
+ * bf16 dS tiles kept in `ds_scratch`
+ * (rt_kernel_attention_bwd_scratch_bytes(batch, seq, heads) bytes of device
+ * memory).  lse2, dvec, ds_scratch and dqkv 16-byte aligned.  Deterministic:
+ * every dQ element is summed in a fixed order (no atomics). */
+RT_API int rt_kernel_attention_bwd_tc(const void* qkv, const void* out, const float* lse2, const void* dout,
+                                      float* dvec, void* ds_scratch, void* dqkv, const float* rope_cos_b,
+                                      const float* rope_sin_b, int batch, int seq, int heads, void* stream);
+RT_API int64_t rt_kernel_attention_bwd_scratch_bytes(int batch, int seq, int heads);
+
 /* Allocation-free variant of rt_kernel_attention_bwd, for callers that cannot
  * call cudaMalloc when they run the backward pass (device memory owned by
  * another allocator, or a loop that must not take cudaMalloc's implicit device

@@ -111,6 +111,9 @@ SIGNATURES: dict[str, tuple] = {
     "rt_kernel_attention_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "rt_kernel_attention_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_int, c_int, c_int, c_void_p]),
+    "rt_kernel_attention_bwd_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "rt_kernel_attention_bwd_scratch_bytes": (c_int64, [c_int, c_int, c_int]),
     "rt_kernel_attention_bwd_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                                 c_void_p, c_int, c_int, c_int, c_void_p]),
     "rt_kernel_rmsnorm_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),

@@ -131,21 +131,26 @@ __device__ __forceinline__ void rope_bwd_frag(float (&acc)[16][4], int pos_a, in
 }
 
 // ------------------------------------------------------ backward: prepare
-// Dv[b, h, s] = sum_e dO[s, h*128 + e] * O[s, h*128 + e]   (one warp per (token, head))
+// Dv[b, h, s] = sum_e dO[s, h*128 + e] * O[s, h*128 + e]: 16 lanes per (token,
+// head), 8 elements (16 B) each, two (token, head) pairs per warp.
 __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ O, int64_t ldo,
                                     const __nv_bfloat16* __restrict__ dO, int64_t lddo, float* __restrict__ Dv,
                                     int M, int S, int nh) {
-  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (wid >= M * nh) return;
-  const int m = wid / nh, h = wid % nh;
-  const uint2 o = *reinterpret_cast<const uint2*>(O + static_cast<int64_t>(m) * ldo + h * HD + lane * 4);
-  const uint2 d = *reinterpret_cast<const uint2*>(dO + static_cast<int64_t>(m) * lddo + h * HD + lane * 4);
-  float s = bf16lo(o.x) * bf16lo(d.x) + bf16hi(o.x) * bf16hi(d.x) + bf16lo(o.y) * bf16lo(d.y) +
-            bf16hi(o.y) * bf16hi(d.y);
+  const int gid = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;  // (token, head) index
+  const int l16 = threadIdx.x & 15;
+  const bool live = gid < M * nh;
+  const int m = live ? gid / nh : 0, h = live ? gid % nh : 0;
+  float s = 0.f;
+  if (live) {
+    const uint4 o = __ldg(reinterpret_cast<const uint4*>(O + static_cast<int64_t>(m) * ldo + h * HD) + l16);
+    const uint4 d = __ldg(reinterpret_cast<const uint4*>(dO + static_cast<int64_t>(m) * lddo + h * HD) + l16);
+    s = bf16lo(o.x) * bf16lo(d.x) + bf16hi(o.x) * bf16hi(d.x) + bf16lo(o.y) * bf16lo(d.y) +
+        bf16hi(o.y) * bf16hi(d.y) + bf16lo(o.z) * bf16lo(d.z) + bf16hi(o.z) * bf16hi(d.z) +
+        bf16lo(o.w) * bf16lo(d.w) + bf16hi(o.w) * bf16hi(d.w);
+  }
 #pragma unroll
-  for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) {
+  for (int off = 8; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (live && l16 == 0) {
     const int b = m / S, pos = m % S;
     Dv[(static_cast<int64_t>(b) * nh + h) * S + pos] = s;
   }
@@ -412,6 +417,15 @@ bool g_attr_done = false;
 
 }  // namespace
 
+int attn_bwd_rowsum(const AttnArgs& a, cudaStream_t s) {
+  if (a.ldo % 8 != 0 || a.lddo % 8 != 0) return -1;
+  const int M = a.batch * a.S;
+  const int64_t threads = static_cast<int64_t>(M) * a.heads * 16;
+  attn_bwd_dot_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, s>>>(a.out, a.ldo, a.dout, a.lddo, a.dvec, M,
+                                                                              a.S, a.heads);
+  return cudaGetLastError();
+}
+
 int attn_backward(const AttnArgs& a, cudaStream_t s) {
   if (a.S % 128 != 0 || a.hd != HD || a.D != a.heads * HD) return -1;
   if (!g_attr_done) {
@@ -421,9 +435,8 @@ int attn_backward(const AttnArgs& a, cudaStream_t s) {
   }
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   const float scale_log2 = scale * 1.4426950408889634f;
-  const int M = a.batch * a.S;
-  const int warps = M * a.heads;
-  attn_bwd_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>(a.out, a.ldo, a.dout, a.lddo, a.dvec, M, a.S, a.heads);
+  const int rc = attn_bwd_rowsum(a, s);
+  if (rc) return rc;
   dim3 grid(a.heads, a.batch, a.S / BWD_B);
   attn_bwd_dkdv_kernel<<<grid, BWD_NT, BWD_SMEM, s>>>(a.qkv, a.ldq, a.D, a.dout, a.lddo, a.lse2, a.dvec, a.dqkv,
                                                       a.lddq, a.S, a.heads, scale, scale_log2, a.rope_cos_b,

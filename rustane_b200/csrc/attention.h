@@ -22,11 +22,19 @@ struct AttnArgs {
   int64_t lddq = 0;
   const float* rope_cos_b = nullptr;  // [hd/2][S]
   const float* rope_sin_b = nullptr;
-  int* err = nullptr;  // device error word (bounded-wait timeouts of the tcgen05 kernel)
+  int* err = nullptr;  // device error word (bounded-wait timeouts of the tcgen05 kernels)
+  // tcgen05 backward: dS^T tiles, attn_bwd_scratch_bytes(batch, S, heads) bytes, 16-B aligned
+  __nv_bfloat16* ds_scratch = nullptr;
 };
 
 // Forward on tcgen05 / TMEM (attention_tc.cu).
 int attn_forward(const AttnArgs& a, cudaStream_t s);
+// Backward with mma.sync (attention.cu): needs only the dvec scratch.
 int attn_backward(const AttnArgs& a, cudaStream_t s);
+// Backward on tcgen05 / TMEM (attention_bwd_tc.cu): needs dvec and ds_scratch.
+int attn_backward_tc(const AttnArgs& a, cudaStream_t s);
+size_t attn_bwd_scratch_bytes(int batch, int S, int heads);
+// rowsum(dO * O) per (sequence, head, query) into a.dvec (attention.cu).
+int attn_bwd_rowsum(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace rt

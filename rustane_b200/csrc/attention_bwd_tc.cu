@@ -1,0 +1,645 @@
+// Causal attention backward on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Same semantics as the mma.sync kernels of attention.cu (sdpaBwd1 / sdpaBwd2,
+// crates/engine/src/kernels/sdpa_bwd.rs:44-162, RoPE backward layer.rs:1880-1897):
+//   P = exp2(S * scale_log2 - lse2),  dP = dO V^T,  dS = P * (dP - rowsum(dO * O)),
+//   dV = P^T dO,  dK = scale * dS^T Q,  dQ = scale * dS K,
+// then the RoPE backward rotation of dK and dQ.  Two kernels:
+//
+// attn_bwd_kv_tc_kernel — one CTA per (head, sequence, block of 128 keys),
+// looping over the 64-query sub-blocks at or after the keys (causal):
+//   warp 0      TMA producer: K and V once, then Q_t, dO_t (64 x 128) and the
+//               per-query statistics lse2 / rowsum into a three-deep ring;
+//   warp 1      one lane issues the MMAs: S^T_t = K Q_t^T and dP^T_t = V dO_t^T
+//               into double-buffered TMEM tiles (128 keys x 64 queries), then
+//               dV += P^T_t dO_t and dK += dS^T_t Q_t into TMEM accumulators;
+//               S^T / dP^T of sub-block t+1 are issued before dV / dK of t, so
+//               the tensor pipe works while the elementwise warps handle t;
+//   warp 2      owns the TMEM allocation (512 columns);
+//   warp 3      stores each dS^T tile (bf16) to the scratch with TMA, for the dQ kernel;
+//   warps 4-11  elementwise: two threads per key row (TMEM lane = key), 32
+//               queries each: P^T = exp2(S^T * scale_log2 - lse2) (causal mask),
+//               dS^T = P^T * (dP^T - rowsum), both written in bf16 into shared
+//               memory in the 128-byte-swizzled K-major layout the MMA reads;
+//               at the end dV and dK (scale, RoPE backward) go from TMEM through
+//               swizzled shared-memory tiles to dqkv by TMA stores.
+//
+// attn_bwd_dq_tc_kernel — one CTA per (head, sequence, block of 128 queries):
+//   dQ = sum over key blocks j of dS_j K_j (both operands MN-major in shared
+//   memory: dS^T tiles as stored, K as laid out in qkv), accumulated in TMEM;
+//   epilogue scale + RoPE backward -> shared memory -> TMA store into dqkv (the
+//   RoPE tables are read while the MMAs run).  The dS scratch replaces atomics:
+//   every dQ element is summed in a fixed order, so the result is deterministic.
+//
+// All waits are bounded; a timeout sets the device error word and the CTA drains.
+#include "attention.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rt {
+namespace {
+
+constexpr int kHd = 128;
+constexpr int kKeys = 128;                     // keys per kv CTA (and per dQ step)
+constexpr int kSub = 64;                       // queries per sub-block
+constexpr int kKvTile = kKeys * kHd * 2;       // 32 KB: two 64-column atoms of 128 rows
+constexpr int kKvAtom = kKvTile / 2;           // 16 KB
+constexpr int kQTile = kSub * kHd * 2;         // 16 KB: two 64-column atoms of 64 rows
+constexpr int kQAtom = kQTile / 2;             // 8 KB
+constexpr int kPTile = kKeys * kSub * 2;       // 16 KB: 128 key rows x 64 queries, one atom
+constexpr int kQStages = 3;                    // Q / dO / statistics ring depth
+constexpr int kKvThreads = 384;
+constexpr int kDqThreads = 256;
+constexpr int kDqStages = 3;
+
+struct KvSmem {
+  static constexpr int K = 0;
+  static constexpr int V = K + kKvTile;
+  static constexpr int Q = V + kKvTile;               // [kQStages]
+  static constexpr int DO = Q + kQStages * kQTile;     // [kQStages]
+  static constexpr int P = DO + kQStages * kQTile;     // [2]
+  static constexpr int DS = P + 2 * kPTile;            // [2]
+  static constexpr int L = DS + 2 * kPTile;            // float [kQStages][64] lse2
+  static constexpr int DV = L + kQStages * kSub * 4;   // float [kQStages][64] rowsum(dO * O)
+  static constexpr int BAR = DV + kQStages * kSub * 4;
+  static constexpr int BYTES = BAR + 256 + 1024;
+};
+static_assert(KvSmem::BYTES <= 232448, "kv kernel shared memory");
+
+enum KvBar : int {
+  kKvFull = 0,
+  kQFull = 1,     // [kQStages] Q, dO, lse2, rowsum of a sub-block
+  kQEmpty = 4,    // [kQStages]
+  kSFull = 7,     // [2] S^T in TMEM
+  kSFree = 9,     // [2]
+  kDpFull = 11,   // [2] dP^T in TMEM
+  kDpFree = 13,   // [2]
+  kPFull = 15,    // [2] P^T in shared memory
+  kPFree = 17,    // [2]
+  kDsFull = 19,   // [2] dS^T in shared memory
+  kDsFree = 21,   // [2] dK MMA done and the tile stored
+  kAccFull = 23,
+  kKvDrain = 24,
+  kKvNumBars = 25
+};
+
+struct DqSmem {
+  static constexpr int STAGE = 2 * kKvTile;  // dS (two 64-query tiles of 128 keys) + K_j
+  static constexpr int BAR = kDqStages * STAGE;
+  static constexpr int BYTES = BAR + 128 + 1024;
+};
+
+// 2-D tiled bulk tensor store shared -> global (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Plain (untiled) bulk copy global -> shared, completion on an mbarrier; 16-B aligned, size % 16 == 0.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 32 values as bf16 into chunks 4c .. 4c+3 of row r of a 128-byte-swizzled tile (row base `row`).
+__device__ __forceinline__ void store_chunk32(uint8_t* row, int c, int r, const float (&v)[32]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    *reinterpret_cast<uint4*>(row + (((c * 4 + u) ^ (r & 7)) << 4)) =
+        make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                   pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+}
+
+// ------------------------------------------------------------------ dK, dV
+__global__ void __launch_bounds__(kKvThreads, 1)
+    attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                          const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_ds,
+                          const __grid_constant__ CUtensorMap tm_out, const float* __restrict__ lse2,
+                          const float* __restrict__ rowsum, int D, int S, int nh, float scale, float scale_log2,
+                          const float* __restrict__ cosb, const float* __restrict__ sinb, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + KvSmem::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kKvNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, b = blockIdx.y, j = blockIdx.z;  // key block 0 has the most work: dispatched first
+  const int nsub = S / kSub, nkb = S / kKeys;
+  const int t0 = 2 * j;           // first sub-block at or after the keys
+  const int n = nsub - t0;        // sub-blocks this CTA visits
+  const int tok0 = b * S;
+  const int k0 = j * kKeys;
+  const int bh = b * nh + h;
+  const int64_t stat0 = static_cast<int64_t>(bh) * S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[kKvFull], 1);
+    for (int i = 0; i < kQStages; ++i) {
+      mbar_init(&bar[kQFull + i], 1);
+      mbar_init(&bar[kQEmpty + i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar[kSFull + i], 1);
+      mbar_init(&bar[kSFree + i], 8);
+      mbar_init(&bar[kDpFull + i], 1);
+      mbar_init(&bar[kDpFree + i], 8);
+      mbar_init(&bar[kPFull + i], 8);
+      mbar_init(&bar[kPFree + i], 1);
+      mbar_init(&bar[kDsFull + i], 8);
+      mbar_init(&bar[kDsFree + i], 2);
+    }
+    mbar_init(&bar[kAccFull], 1);
+    mbar_init(&bar[kKvDrain], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_kv);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_ds);
+    tma_prefetch_desc(&tm_out);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // TMEM columns: S^T [0,64) [64,128), dP^T [128,192) [192,256), dV [256,384), dK [384,512)
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t kColS = 0, kColDp = 128, kColDv = 256, kColDk = 384;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      const int qc = h * kHd, kc = D + h * kHd, vc = 2 * D + h * kHd;
+      int issued = 0;
+      mbar_arrive_expect_tx(&bar[kKvFull], 2 * kKvTile);
+      tma_load_2d(smem + KvSmem::K, &tm_kv, &bar[kKvFull], kc, tok0 + k0);
+      tma_load_2d(smem + KvSmem::K + kKvAtom, &tm_kv, &bar[kKvFull], kc + 64, tok0 + k0);
+      tma_load_2d(smem + KvSmem::V, &tm_kv, &bar[kKvFull], vc, tok0 + k0);
+      tma_load_2d(smem + KvSmem::V + kKvAtom, &tm_kv, &bar[kKvFull], vc + 64, tok0 + k0);
+      for (int t = 0; t < n; ++t) {
+        const int st = t % kQStages;
+        const uint32_t ph = (t / kQStages) & 1;
+        if (!mbar_wait(&bar[kQEmpty + st], ph ^ 1) || *abort_flag) {
+          set_error(err, kDevTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        const int q0 = (t0 + t) * kSub;
+        uint64_t* fb = &bar[kQFull + st];
+        mbar_arrive_expect_tx(fb, 2 * kQTile + 2 * kSub * 4);
+        uint8_t* sq = smem + KvSmem::Q + st * kQTile;
+        uint8_t* sd = smem + KvSmem::DO + st * kQTile;
+        tma_load_2d(sq, &tm_q, fb, qc, tok0 + q0);
+        tma_load_2d(sq + kQAtom, &tm_q, fb, qc + 64, tok0 + q0);
+        tma_load_2d(sd, &tm_do, fb, h * kHd, tok0 + q0);
+        tma_load_2d(sd + kQAtom, &tm_do, fb, h * kHd + 64, tok0 + q0);
+        bulk_load(smem + KvSmem::L + st * kSub * 4, lse2 + stat0 + q0, kSub * 4, fb);
+        bulk_load(smem + KvSmem::DV + st * kSub * 4, rowsum + stat0 + q0, kSub * 4, fb);
+        issued = t + 1;
+      }
+      if (*abort_flag) {  // let copies still in flight land before the CTA exits
+        mbar_wait(&bar[kKvFull], 0);
+        for (int t = (issued > kQStages ? issued - kQStages : 0); t < issued; ++t)
+          mbar_wait(&bar[kQFull + t % kQStages], (t / kQStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc_s = idesc_bf16_f32(kKeys, kSub, false, false);  // K / V rows, Q / dO rows
+      constexpr uint32_t idesc_a = idesc_bf16_f32(kKeys, kHd, false, true);   // P^T / dS^T, dO / Q hd-contiguous
+      const uint32_t sk = smem_u32(smem + KvSmem::K), sv = smem_u32(smem + KvSmem::V);
+      bool ok = mbar_wait(&bar[kKvFull], 0);
+      auto issue_s = [&](int t) -> bool {  // S^T_t and dP^T_t
+        const int st = t & 1, qs = t % kQStages;
+        const uint32_t ph = (t >> 1) & 1;
+        if (!mbar_wait(&bar[kQFull + qs], (t / kQStages) & 1) || !mbar_wait(&bar[kSFree + st], ph ^ 1) || *abort_flag)
+          return false;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(smem + KvSmem::Q + qs * kQTile);
+        const uint32_t sd = smem_u32(smem + KvSmem::DO + qs * kQTile);
+#pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          const uint32_t ka = (kk >> 2) * kKvAtom + (kk & 3) * 32, kb = (kk >> 2) * kQAtom + (kk & 3) * 32;
+          umma_bf16(tmem + kColS + st * kSub, smem_desc_sw128(sk + ka, 16, 1024), smem_desc_sw128(sq + kb, 16, 1024),
+                    idesc_s, kk != 0 ? 1u : 0u);
+        }
+        umma_commit(&bar[kSFull + st]);
+        if (!mbar_wait(&bar[kDpFree + st], ph ^ 1) || *abort_flag) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          const uint32_t ka = (kk >> 2) * kKvAtom + (kk & 3) * 32, kb = (kk >> 2) * kQAtom + (kk & 3) * 32;
+          umma_bf16(tmem + kColDp + st * kSub, smem_desc_sw128(sv + ka, 16, 1024), smem_desc_sw128(sd + kb, 16, 1024),
+                    idesc_s, kk != 0 ? 1u : 0u);
+        }
+        umma_commit(&bar[kDpFull + st]);
+        return true;
+      };
+      ok = ok && issue_s(0);
+      for (int t = 0; ok && t < n; ++t) {
+        if (t + 1 < n && !issue_s(t + 1)) {
+          ok = false;
+          break;
+        }
+        const int st = t & 1, qs = t % kQStages;
+        const uint32_t ph = (t >> 1) & 1;
+        const uint32_t sq = smem_u32(smem + KvSmem::Q + qs * kQTile);
+        const uint32_t sd = smem_u32(smem + KvSmem::DO + qs * kQTile);
+        // dV += P^T dO: P^T K-major over the 64 queries, dO hd-contiguous (two 64-wide blocks 8 KB apart)
+        if (!mbar_wait(&bar[kPFull + st], ph) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sp = smem_u32(smem + KvSmem::P + st * kPTile);
+#pragma unroll
+        for (int kk = 0; kk < kSub / 16; ++kk)
+          umma_bf16(tmem + kColDv, smem_desc_sw128(sp + kk * 32, 16, 1024), smem_desc_sw128(sd + kk * 2048, kQAtom, 1024),
+                    idesc_a, (t | kk) != 0 ? 1u : 0u);
+        umma_commit(&bar[kPFree + st]);
+        // dK += dS^T Q
+        if (!mbar_wait(&bar[kDsFull + st], ph) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sds = smem_u32(smem + KvSmem::DS + st * kPTile);
+#pragma unroll
+        for (int kk = 0; kk < kSub / 16; ++kk)
+          umma_bf16(tmem + kColDk, smem_desc_sw128(sds + kk * 32, 16, 1024),
+                    smem_desc_sw128(sq + kk * 2048, kQAtom, 1024), idesc_a, (t | kk) != 0 ? 1u : 0u);
+        umma_commit(&bar[kDsFree + st]);
+        umma_commit(&bar[kQEmpty + qs]);
+      }
+      if (!ok) {
+        set_error(err, kDevTimeoutMma);
+        *abort_flag = 1;
+      } else {
+        umma_commit(&bar[kAccFull]);
+      }
+      umma_commit(&bar[kKvDrain]);
+      mbar_wait(&bar[kKvDrain], 0);
+    }
+  } else if (warp == 3) {
+    if (lane == 0) {
+      // ------------------------------------------------- dS^T tiles -> scratch
+      // scratch row of (sequence-head bh, key block j, sub-block i): ((bh * nkb + j) * nsub + i) * 128
+      int t = 0;
+      for (; t < n; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(&bar[kDsFull + st], (t >> 1) & 1) || *abort_flag) break;
+        const int row = ((bh * nkb + j) * nsub + t0 + t) * kKeys;
+        tma_store_2d(&tm_ds, smem + KvSmem::DS + st * kPTile, 0, row);
+        bulk_commit();
+        bulk_wait_read_all();
+        mbar_arrive(&bar[kDsFree + st]);
+      }
+      if (t < n) {
+        set_error(err, kDevTimeoutEpilogue);
+        *abort_flag = 1;
+      }
+      bulk_wait_all();
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- elementwise
+    const int qw = warp & 3;            // TMEM lane quadrant: key rows 32 qw ..
+    const int hh = (warp - 4) >> 2;     // query columns [32 hh, 32 hh + 32) of a sub-block
+    const int r = qw * 32 + lane;       // key row within the block
+    const int kpos = k0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
+    const float* sl = reinterpret_cast<const float*>(smem + KvSmem::L);
+    const float* sdv = reinterpret_cast<const float*>(smem + KvSmem::DV);
+    bool ok = true;
+    auto wait = [&](uint64_t* bb, uint32_t parity) {
+      bool w = ok && !*abort_flag && mbar_wait(bb, parity);
+      w = __all_sync(0xffffffffu, w);
+      if (!w) {
+        ok = false;
+        *abort_flag = 1;
+      }
+      return w;
+    };
+    for (int t = 0; ok && t < n; ++t) {
+      const int st = t & 1, qs = t % kQStages;
+      const uint32_t ph = (t >> 1) & 1;
+      const int q0 = (t0 + t) * kSub + hh * 32;  // first query of this thread's 32 columns
+      if (!wait(&bar[kQFull + qs], (t / kQStages) & 1) || !wait(&bar[kSFull + st], ph)) break;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld32(tmem + kColS + st * kSub + lane_off + hh * 32, v);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kSFree + st]);
+      const float* L = sl + qs * kSub + hh * 32;
+      float p[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float pe = exp2f(__uint_as_float(v[e]) * scale_log2 - L[e]);
+        p[e] = q0 + e >= kpos ? pe : 0.f;  // causal: query before key -> 0
+      }
+      // P^T row r, columns 32 hh .. +31: 4 chunks of 16 B, chunk c at (c ^ r % 8) * 16
+      if (!wait(&bar[kPFree + st], ph ^ 1)) break;
+      uint8_t* prow = smem + KvSmem::P + st * kPTile + r * 128;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(prow + (((hh * 4 + u) ^ (r & 7)) << 4)) =
+            make_uint4(pack_bf16x2(p[8 * u], p[8 * u + 1]), pack_bf16x2(p[8 * u + 2], p[8 * u + 3]),
+                       pack_bf16x2(p[8 * u + 4], p[8 * u + 5]), pack_bf16x2(p[8 * u + 6], p[8 * u + 7]));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kPFull + st]);
+      if (!wait(&bar[kDpFull + st], ph)) break;
+      tc_fence_after();
+      tmem_ld32(tmem + kColDp + st * kSub + lane_off + hh * 32, v);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kDpFree + st]);
+      const float* Dd = sdv + qs * kSub + hh * 32;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) p[e] = p[e] * (__uint_as_float(v[e]) - Dd[e]);
+      if (!wait(&bar[kDsFree + st], ph ^ 1)) break;
+      uint8_t* drow = smem + KvSmem::DS + st * kPTile + r * 128;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(drow + (((hh * 4 + u) ^ (r & 7)) << 4)) =
+            make_uint4(pack_bf16x2(p[8 * u], p[8 * u + 1]), pack_bf16x2(p[8 * u + 2], p[8 * u + 3]),
+                       pack_bf16x2(p[8 * u + 4], p[8 * u + 5]), pack_bf16x2(p[8 * u + 6], p[8 * u + 7]));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kDsFull + st]);
+    }
+    // RoPE tables of this key position for head-dim pairs [32 hh, 32 hh + 32), loaded
+    // while the last MMAs run
+    float rc[32], rs[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      rc[i] = __ldg(cosb + static_cast<int64_t>(hh * 32 + i) * S + kpos);
+      rs[i] = __ldg(sinb + static_cast<int64_t>(hh * 32 + i) * S + kpos);
+    }
+    if (ok) wait(&bar[kAccFull], 0);
+    if (!ok && lane == 0) set_error(err, kDevTimeoutEpilogue);
+    if (ok) {
+      tc_fence_after();
+      // dK (scale, RoPE backward) and dV rows -> bf16 tiles in the (now idle) Q / dO ring, 128-byte
+      // swizzled, head-dim columns [64 hh, 64 hh + 64) = atom hh; then TMA stores into dqkv
+      uint8_t* tk = smem + KvSmem::Q + hh * kKvAtom + r * 128;
+      uint8_t* tv = smem + KvSmem::Q + kKvTile + hh * kKvAtom + r * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        float f[32];
+        tmem_ld32(tmem + kColDv + lane_off + hh * 64 + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]);
+        store_chunk32(tv, c, r, f);
+        tmem_ld32(tmem + kColDk + lane_off + hh * 64 + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float d0 = __uint_as_float(v[e]) * scale, d1 = __uint_as_float(v[e + 1]) * scale;
+          const float cc = rc[c * 16 + e / 2], ss = rs[c * 16 + e / 2];
+          f[e] = cc * d0 + ss * d1;
+          f[e + 1] = -ss * d0 + cc * d1;
+        }
+        store_chunk32(tk, c, r, f);
+      }
+      fence_proxy_async_smem();
+    }
+    // every elementwise warp reaches the named barrier (a failed warp skips only its work)
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (threadIdx.x == 128 && !*abort_flag) {
+      const int y = tok0 + k0;
+      tma_store_2d(&tm_out, smem + KvSmem::Q, D + h * kHd, y);
+      tma_store_2d(&tm_out, smem + KvSmem::Q + kKvAtom, D + h * kHd + 64, y);
+      tma_store_2d(&tm_out, smem + KvSmem::Q + kKvTile, 2 * D + h * kHd, y);
+      tma_store_2d(&tm_out, smem + KvSmem::Q + kKvTile + kKvAtom, 2 * D + h * kHd + 64, y);
+      bulk_commit();
+      bulk_wait_read_all();
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------- dQ
+__global__ void __launch_bounds__(kDqThreads, 1)
+    attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_ds2,
+                          const __grid_constant__ CUtensorMap tm_out, int D, int S, int nh, float scale,
+                          const float* __restrict__ cosb, const float* __restrict__ sinb, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DqSmem::BAR);  // full[3], empty[3], acc, drain
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2 * kDqStages + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* full = bar;
+  uint64_t* empty = bar + kDqStages;
+  uint64_t* acc = bar + 2 * kDqStages;
+  uint64_t* drain = acc + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = gridDim.z - 1 - blockIdx.z;  // heaviest query blocks first
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int nb = qb + 1;  // key blocks 0 .. qb
+  const int nsub = S / kSub, nkb = S / kKeys;
+  const int tok0 = b * S;
+  const int bh = b * nh + h;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDqStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_kv);
+    tma_prefetch_desc(&tm_ds2);
+    tma_prefetch_desc(&tm_out);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int kc = D + h * kHd;
+      int issued = 0;
+      for (int jj = 0; jj < nb; ++jj) {
+        const int st = jj % kDqStages;
+        const uint32_t ph = (jj / kDqStages) & 1;
+        if (!mbar_wait(&empty[st], ph ^ 1) || *abort_flag) {
+          set_error(err, kDevTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* s = smem + st * DqSmem::STAGE;
+        mbar_arrive_expect_tx(&full[st], DqSmem::STAGE);
+        // dS^T of sub-blocks 2 qb and 2 qb + 1 (consecutive 128-row tiles of the scratch)
+        tma_load_2d(s, &tm_ds2, &full[st], 0, ((bh * nkb + jj) * nsub + 2 * qb) * kKeys);
+        tma_load_2d(s + kKvTile, &tm_kv, &full[st], kc, tok0 + jj * kKeys);
+        tma_load_2d(s + kKvTile + kKvAtom, &tm_kv, &full[st], kc + 64, tok0 + jj * kKeys);
+        issued = jj + 1;
+      }
+      if (*abort_flag)
+        for (int jj = (issued > kDqStages ? issued - kDqStages : 0); jj < issued; ++jj)
+          mbar_wait(&full[jj % kDqStages], (jj / kDqStages) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // dQ (128 queries x 128) += dS_j (queries contiguous) K_j (head dim contiguous); K = 128 keys
+      constexpr uint32_t idesc = idesc_bf16_f32(kKeys, kHd, true, true);
+      bool ok = true;
+      for (int jj = 0; jj < nb; ++jj) {
+        const int st = jj % kDqStages;
+        if (!mbar_wait(&full[st], (jj / kDqStages) & 1) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + st * DqSmem::STAGE), sb = sa + kKvTile;
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk)
+          umma_bf16(tmem, smem_desc_sw128(sa + kk * 2048, kKvAtom, 1024), smem_desc_sw128(sb + kk * 2048, kKvAtom, 1024),
+                    idesc, (jj | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[st]);
+      }
+      if (!ok) {
+        set_error(err, kDevTimeoutMma);
+        *abort_flag = 1;
+      } else {
+        umma_commit(acc);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0);
+    }
+  } else if (warp >= 4) {
+    const int qw = warp & 3;
+    const int r = qw * 32 + lane;  // query row within the block
+    const int qpos = qb * kKeys + r;
+    const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
+    float rc[64], rs[64];  // RoPE tables of this query position, loaded while the MMAs run
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      rc[i] = __ldg(cosb + static_cast<int64_t>(i) * S + qpos);
+      rs[i] = __ldg(sinb + static_cast<int64_t>(i) * S + qpos);
+    }
+    bool w = !*abort_flag && mbar_wait(acc, 0);
+    w = __all_sync(0xffffffffu, w);
+    if (!w) {
+      if (lane == 0) set_error(err, kDevTimeoutEpilogue);
+      *abort_flag = 1;
+    }
+    // every epilogue warp reaches the named barrier (a failed warp skips only its work)
+    if (w) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        float f[32];
+        tmem_ld32(tmem + lane_off + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float d0 = __uint_as_float(v[e]) * scale, d1 = __uint_as_float(v[e + 1]) * scale;
+          const float cc = rc[c * 16 + e / 2], ss = rs[c * 16 + e / 2];
+          f[e] = cc * d0 + ss * d1;
+          f[e + 1] = -ss * d0 + cc * d1;
+        }
+        // dQ tile in stage 0 (idle once the accumulator is complete): atom c / 2, chunks 4 (c % 2) ..
+        store_chunk32(smem + (c >> 1) * kKvAtom + r * 128, c & 1, r, f);
+      }
+      fence_proxy_async_smem();
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+    if (threadIdx.x == 128 && !*abort_flag) {
+      const int y = tok0 + qb * kKeys;
+      tma_store_2d(&tm_out, smem, h * kHd, y);
+      tma_store_2d(&tm_out, smem + kKvAtom, h * kHd + 64, y);
+      bulk_commit();
+      bulk_wait_read_all();
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+}  // namespace
+
+size_t attn_bwd_scratch_bytes(int batch, int S, int heads) {
+  return static_cast<size_t>(batch) * heads * S * S * 2;
+}
+
+int attn_backward_tc(const AttnArgs& a, cudaStream_t s) {
+  if (a.S % kKeys != 0 || a.hd != kHd || a.D != a.heads * kHd || a.ldq % 8 != 0 || a.lddo % 8 != 0 ||
+      a.lddq % 8 != 0 || !a.ds_scratch)
+    return -1;
+  if ((reinterpret_cast<uintptr_t>(a.lse2) | reinterpret_cast<uintptr_t>(a.dvec) |
+       reinterpret_cast<uintptr_t>(a.ds_scratch) | reinterpret_cast<uintptr_t>(a.dqkv)) & 15)
+    return -1;
+  const uint64_t M = static_cast<uint64_t>(a.batch) * a.S;
+  const uint64_t ds_rows = static_cast<uint64_t>(a.batch) * a.heads * a.S * a.S / kSub;
+  CUtensorMap tm_kv, tm_q, tm_do, tm_ds, tm_ds2, tm_out;
+  if (!make_tmap_bf16(&tm_kv, a.qkv, 3 * static_cast<uint64_t>(a.D), M, a.ldq, 64, kKeys) ||
+      !make_tmap_bf16(&tm_q, a.qkv, 3 * static_cast<uint64_t>(a.D), M, a.ldq, 64, kSub) ||
+      !make_tmap_bf16(&tm_do, a.dout, static_cast<uint64_t>(a.D), M, a.lddo, 64, kSub) ||
+      !make_tmap_bf16(&tm_ds, a.ds_scratch, kSub, ds_rows, kSub, 64, kKeys) ||
+      !make_tmap_bf16(&tm_ds2, a.ds_scratch, kSub, ds_rows, kSub, 64, 2 * kKeys) ||
+      !make_tmap_bf16(&tm_out, a.dqkv, 3 * static_cast<uint64_t>(a.D), M, a.lddq, 64, kKeys))
+    return -3;
+  static const cudaError_t attr1 =
+      cudaFuncSetAttribute(attn_bwd_kv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KvSmem::BYTES);
+  static const cudaError_t attr2 =
+      cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem::BYTES);
+  if (attr1 != cudaSuccess) return attr1;
+  if (attr2 != cudaSuccess) return attr2;
+  int rc = attn_bwd_rowsum(a, s);
+  if (rc) return rc;
+  const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
+  const float scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid(a.heads, a.batch, a.S / kKeys);
+  attn_bwd_kv_tc_kernel<<<grid, kKvThreads, KvSmem::BYTES, s>>>(tm_kv, tm_q, tm_do, tm_ds, tm_out, a.lse2, a.dvec,
+                                                               a.D, a.S, a.heads, scale, scale_log2, a.rope_cos_b,
+                                                               a.rope_sin_b, a.err);
+  attn_bwd_dq_tc_kernel<<<grid, kDqThreads, DqSmem::BYTES, s>>>(tm_kv, tm_ds2, tm_out, a.D, a.S, a.heads, scale,
+                                                               a.rope_cos_b, a.rope_sin_b, a.err);
+  return cudaGetLastError();
+}
+
+}  // namespace rt

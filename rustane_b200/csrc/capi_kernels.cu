@@ -98,6 +98,38 @@ RT_API int rt_kernel_attention_bwd(const void* qkv, const void* out, const float
   return map_rc(rt::attn_backward(a, st(stream)));
 }
 
+RT_API int rt_kernel_attention_bwd_tc(const void* qkv, const void* out, const float* lse2, const void* dout,
+                                      float* dvec, void* ds_scratch, void* dqkv, const float* rope_cos_b,
+                                      const float* rope_sin_b, int batch, int seq, int heads, void* stream) {
+  if (!qkv || !out || !lse2 || !dout || !dvec || !ds_scratch || !dqkv || !rope_cos_b || !rope_sin_b)
+    return RT_ERR_ARG;
+  rt::AttnArgs a;
+  a.batch = batch;
+  a.S = seq;
+  a.heads = heads;
+  a.hd = 128;
+  a.D = heads * 128;
+  a.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  a.ldq = 3 * a.D;
+  a.out = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(out));
+  a.ldo = a.D;
+  a.lse2 = const_cast<float*>(lse2);
+  a.dout = static_cast<const __nv_bfloat16*>(dout);
+  a.lddo = a.D;
+  a.dvec = dvec;
+  a.ds_scratch = static_cast<__nv_bfloat16*>(ds_scratch);
+  a.dqkv = static_cast<__nv_bfloat16*>(dqkv);
+  a.lddq = 3 * a.D;
+  a.rope_cos_b = rope_cos_b;
+  a.rope_sin_b = rope_sin_b;
+  return map_rc(rt::attn_backward_tc(a, st(stream)));
+}
+
+RT_API int64_t rt_kernel_attention_bwd_scratch_bytes(int batch, int seq, int heads) {
+  if (batch <= 0 || seq <= 0 || heads <= 0) return 0;
+  return static_cast<int64_t>(rt::attn_bwd_scratch_bytes(batch, seq, heads));
+}
+
 RT_API int rt_kernel_rmsnorm_fwd(const float* x, const float* gamma, void* out_bf16, float* rms_inv, int M, int D,
                                  void* stream) {
   return map_rc(rt::rmsnorm_fwd(x, gamma, static_cast<__nv_bfloat16*>(out_bf16), rms_inv, M, D, st(stream)));

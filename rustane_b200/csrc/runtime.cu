@@ -683,9 +683,9 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     a.batch = batch; a.S = S; a.heads = cfg.heads; a.hd = cfg.hd; a.D = D;
     a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
     a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv[p]; a.lddq = 3 * D;
-    a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b; a.err = c->d_err;
+    a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b; a.err = c->d_err; a.ds_scratch = c->attn_ds;
     const double fl = 2.5 * 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
-    RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward(a, ms); }), "attention bwd");
+    RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward_tc(a, ms); }), "attention bwd");
   }
   cudaEventRecord(c->ev_attn[l], ms);
   cudaStreamWaitEvent(ds, c->ev_attn[l], 0);
@@ -983,9 +983,10 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
     }
     c->da = dalloc<bf16>(c, M * D);
     c->dvec = dalloc<float>(c, M * cfg.heads);
+    c->attn_ds = dalloc<bf16>(c, static_cast<int64_t>(rt::attn_bwd_scratch_bytes(max_batch, S, cfg.heads) / 2));
     c->dgamma_part = dalloc<float>(c, int64_t(rt::rmsnorm_bwd_blocks(static_cast<int>(M))) * D);
     for (void* p : {(void*)c->dl, (void*)c->dy_b, (void*)c->dx_tmp, (void*)c->dx2, (void*)c->da, (void*)c->dvec,
-                    (void*)c->dgamma_part})
+                    (void*)c->attn_ds, (void*)c->dgamma_part})
       need(p);
   }
   alloc_token_batch(c, c->io);

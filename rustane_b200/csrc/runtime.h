@@ -106,6 +106,7 @@ struct rt_ctx {
   rt::bf16* dqkv[2] = {};  // [M, 3D]
   rt::bf16* da = nullptr;  // [M, D]
   float* dvec = nullptr;     // [B, heads, S]
+  rt::bf16* attn_ds = nullptr;  // dS^T tiles of the tcgen05 attention backward (B * heads * S * S)
   float* dgamma_part = nullptr;
 
   // tokens and the embedding-scatter segments: `io` is refilled by every call

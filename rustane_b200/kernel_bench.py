@@ -1,7 +1,7 @@
 """Single-kernel timing of the LM-step kernels at a chosen shape (CUDA events).
 
     python -m rustane_b200.kernel_bench gemm --m 4096 --n 4096 --k 1536 --b-mn --epi swiglu [--bn -256 | --cublas]
-    python -m rustane_b200.kernel_bench attention --batch 8 --seq 512 --heads 12 [--bwd]
+    python -m rustane_b200.kernel_bench attention --batch 8 --seq 512 --heads 12 [--bwd [--impl tc|mma]]
     python -m rustane_b200.kernel_bench rmsnorm_bwd --m 4096 --d 1536
 
 Prints one JSON line (mean us per launch, TFLOP/s or GB/s).  Buffers come from
@@ -100,11 +100,17 @@ def bench_attention(args):
     dvec = torch.empty(B, H, S, device="cuda")
     dqkv = torch.empty(B * S, 3 * D, device="cuda", dtype=torch.bfloat16)
     cb, sb = torch.rand(64, S, device="cuda"), torch.rand(64, S, device="cuda")
-    bwd = lambda: L.rt_kernel_attention_bwd(qkv.data_ptr(), out.data_ptr(), lse.data_ptr(), dout.data_ptr(),  # noqa
-                                            dvec.data_ptr(), dqkv.data_ptr(), cb.data_ptr(), sb.data_ptr(), B, S, H,
-                                            st)
+    if args.impl == "tc":
+        ds = torch.empty(L.rt_kernel_attention_bwd_scratch_bytes(B, S, H) // 2, device="cuda", dtype=torch.bfloat16)
+        bwd = lambda: L.rt_kernel_attention_bwd_tc(  # noqa
+            qkv.data_ptr(), out.data_ptr(), lse.data_ptr(), dout.data_ptr(), dvec.data_ptr(), ds.data_ptr(),
+            dqkv.data_ptr(), cb.data_ptr(), sb.data_ptr(), B, S, H, st)
+    else:
+        bwd = lambda: L.rt_kernel_attention_bwd(  # noqa
+            qkv.data_ptr(), out.data_ptr(), lse.data_ptr(), dout.data_ptr(), dvec.data_ptr(), dqkv.data_ptr(),
+            cb.data_ptr(), sb.data_ptr(), B, S, H, st)
     us = _time(bwd, args.iters)
-    return {"kernel": "attention_bwd", "B": B, "S": S, "H": H, "us": us, "tflops": 2.5 * fl / us / 1e6}
+    return {"kernel": f"attention_bwd_{args.impl}", "B": B, "S": S, "H": H, "us": us, "tflops": 2.5 * fl / us / 1e6}
 
 
 def bench_rmsnorm_bwd(args):
@@ -144,6 +150,7 @@ def main():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--heads", type=int, default=12)
     ap.add_argument("--bwd", action="store_true")
+    ap.add_argument("--impl", default="tc", choices=["tc", "mma"], help="attention backward kernels")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     fn = {"gemm": bench_gemm, "attention": bench_attention, "rmsnorm_bwd": bench_rmsnorm_bwd}[args.kernel]

@@ -203,23 +203,46 @@ def test_attention_forward(B, S, H, amp):
     assert (lse2 - lse / np.log(2.0)).abs().max().item() < 2e-3
 
 
-@pytest.mark.parametrize("B,S,H", [(2, 256, 2), (1, 512, 3)])
-def test_attention_backward_with_rope(B, S, H):
+def _attn_bwd(impl, qkv, out, lse2, dout, tcb, tsb, B, S, H):
+    D = H * 128
+    dvec = torch.empty(B, H, S, device="cuda")
+    dqkv = torch.full((B * S, 3 * D), float("nan"), device="cuda", dtype=torch.bfloat16)
+    if impl == "tc":
+        nbytes = L.rt_kernel_attention_bwd_scratch_bytes(B, S, H)
+        assert nbytes == B * H * S * S * 2
+        ds = torch.empty(nbytes // 2, device="cuda", dtype=torch.bfloat16)
+        ok(L.rt_kernel_attention_bwd_tc(qkv.data_ptr(), out.data_ptr(), lse2.data_ptr(), dout.data_ptr(),
+                                        dvec.data_ptr(), ds.data_ptr(), dqkv.data_ptr(), tcb.data_ptr(),
+                                        tsb.data_ptr(), B, S, H, stream()))
+    else:
+        ok(L.rt_kernel_attention_bwd(qkv.data_ptr(), out.data_ptr(), lse2.data_ptr(), dout.data_ptr(),
+                                     dvec.data_ptr(), dqkv.data_ptr(), tcb.data_ptr(), tsb.data_ptr(), B, S, H,
+                                     stream()))
+    torch.cuda.synchronize()
+    return dqkv
+
+
+# "tc": tcgen05 / TMEM kernels (the model step's path); "mma": the mma.sync kernels (noalloc entry).
+# S = 128 is one key block (diagonal sub-blocks only); 384 and 1024 make ragged causal work per CTA;
+# amp = 2 gives larger logits (sharper P).
+@pytest.mark.parametrize("impl", ["tc", "mma"])
+@pytest.mark.parametrize("B,S,H,amp", [(2, 256, 2, 1.0), (1, 512, 3, 1.0), (1, 128, 2, 1.0), (3, 384, 1, 1.0),
+                                       (1, 1024, 2, 1.0), (1, 512, 2, 2.0)])
+def test_attention_backward_with_rope(impl, B, S, H, amp):
     from rustane_b200.model import ModelConfig
     D = H * 128
     cfg = ModelConfig.custom(D, 256, H, 1, seq=S, vocab=256)
     _, _, cb, sb = po.Oracle(cfg, 1).rope_tables()
     g = torch.Generator(device="cuda").manual_seed(6)
-    qkv = torch.randn(B * S, 3 * D, generator=g, device="cuda").bfloat16()
+    qkv = (amp * torch.randn(B * S, 3 * D, generator=g, device="cuda")).bfloat16()
     dout = torch.randn(B * S, D, generator=g, device="cuda").bfloat16()
     out = torch.empty(B * S, D, device="cuda", dtype=torch.bfloat16)
     lse2 = torch.empty(B, H, S, device="cuda")
     ok(L.rt_kernel_attention_fwd(qkv.data_ptr(), out.data_ptr(), lse2.data_ptr(), B, S, H, stream()))
-    dvec = torch.empty(B, H, S, device="cuda")
-    dqkv = torch.empty(B * S, 3 * D, device="cuda", dtype=torch.bfloat16)
     tcb, tsb = torch.from_numpy(cb).cuda(), torch.from_numpy(sb).cuda()
-    ok(L.rt_kernel_attention_bwd(qkv.data_ptr(), out.data_ptr(), lse2.data_ptr(), dout.data_ptr(), dvec.data_ptr(),
-                                 dqkv.data_ptr(), tcb.data_ptr(), tsb.data_ptr(), B, S, H, stream()))
+    dqkv = _attn_bwd(impl, qkv, out, lse2, dout, tcb, tsb, B, S, H)
+    if impl == "tc":  # fixed summation order: bitwise repeatable
+        assert torch.equal(_attn_bwd(impl, qkv, out, lse2, dout, tcb, tsb, B, S, H), dqkv)
     x = qkv.float().requires_grad_(True)
     o_ref, _ = _attn_ref(x, B, S, H)
     o_ref.backward(dout.float())
