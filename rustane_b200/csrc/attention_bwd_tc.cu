@@ -8,8 +8,8 @@
 //
 // attn_bwd_kv_tc_kernel — one CTA per (head, sequence, block of 128 keys),
 // looping over the 64-query sub-blocks at or after the keys (causal):
-//   warp 0      TMA producer: K and V once, then Q_t, dO_t (64 x 128) and the
-//               per-query statistics lse2 / rowsum into a three-deep ring;
+//   warp 0      TMA producer: K and V once, then Q_t, dO_t (64 x 128) into a
+//               four-deep ring;
 //   warp 1      one lane issues the MMAs: S^T_t = K Q_t^T and dP^T_t = V dO_t^T
 //               into double-buffered TMEM tiles (128 keys x 64 queries), then
 //               dV += P^T_t dO_t and dK += dS^T_t Q_t into TMEM accumulators;
@@ -20,7 +20,10 @@
 //   warps 4-11  elementwise: two threads per key row (TMEM lane = key), 32
 //               queries each: P^T = exp2(S^T * scale_log2 - lse2) (causal mask),
 //               dS^T = P^T * (dP^T - rowsum), both written in bf16 into shared
-//               memory in the 128-byte-swizzled K-major layout the MMA reads;
+//               memory in the 128-byte-swizzled K-major layout the MMA reads
+//               (one tile each: the MMA that reads tile t finishes long before
+//               tile t+1 is ready); lse2 / rowsum come from L2, one per lane,
+//               passed around by shuffles;
 //               at the end dV and dK (scale, RoPE backward) go from TMEM through
 //               swizzled shared-memory tiles to dqkv by TMA stores.
 //
@@ -47,7 +50,7 @@ constexpr int kKvAtom = kKvTile / 2;           // 16 KB
 constexpr int kQTile = kSub * kHd * 2;         // 16 KB: two 64-column atoms of 64 rows
 constexpr int kQAtom = kQTile / 2;             // 8 KB
 constexpr int kPTile = kKeys * kSub * 2;       // 16 KB: 128 key rows x 64 queries, one atom
-constexpr int kQStages = 3;                    // Q / dO / statistics ring depth
+constexpr int kQStages = 4;                    // Q / dO ring depth
 constexpr int kKvThreads = 384;
 constexpr int kDqThreads = 256;
 constexpr int kDqStages = 3;
@@ -57,30 +60,28 @@ struct KvSmem {
   static constexpr int V = K + kKvTile;
   static constexpr int Q = V + kKvTile;               // [kQStages]
   static constexpr int DO = Q + kQStages * kQTile;     // [kQStages]
-  static constexpr int P = DO + kQStages * kQTile;     // [2]
-  static constexpr int DS = P + 2 * kPTile;            // [2]
-  static constexpr int L = DS + 2 * kPTile;            // float [kQStages][64] lse2
-  static constexpr int DV = L + kQStages * kSub * 4;   // float [kQStages][64] rowsum(dO * O)
-  static constexpr int BAR = DV + kQStages * kSub * 4;
+  static constexpr int P = DO + kQStages * kQTile;     // one P^T tile
+  static constexpr int DS = P + kPTile;                // one dS^T tile
+  static constexpr int BAR = DS + kPTile;
   static constexpr int BYTES = BAR + 256 + 1024;
 };
 static_assert(KvSmem::BYTES <= 232448, "kv kernel shared memory");
 
 enum KvBar : int {
   kKvFull = 0,
-  kQFull = 1,     // [kQStages] Q, dO, lse2, rowsum of a sub-block
-  kQEmpty = 4,    // [kQStages]
-  kSFull = 7,     // [2] S^T in TMEM
-  kSFree = 9,     // [2]
-  kDpFull = 11,   // [2] dP^T in TMEM
-  kDpFree = 13,   // [2]
-  kPFull = 15,    // [2] P^T in shared memory
-  kPFree = 17,    // [2]
-  kDsFull = 19,   // [2] dS^T in shared memory
-  kDsFree = 21,   // [2] dK MMA done and the tile stored
-  kAccFull = 23,
-  kKvDrain = 24,
-  kKvNumBars = 25
+  kQFull = 1,     // [kQStages] Q and dO of a sub-block
+  kQEmpty = 5,    // [kQStages]
+  kSFull = 9,     // [2] S^T in TMEM
+  kSFree = 11,    // [2]
+  kDpFull = 13,   // [2] dP^T in TMEM
+  kDpFree = 15,   // [2]
+  kPFull = 17,    // P^T in shared memory
+  kPFree = 18,
+  kDsFull = 19,   // dS^T in shared memory
+  kDsFree = 20,   // dK MMA done and the tile stored
+  kAccFull = 21,
+  kKvDrain = 22,
+  kKvNumBars = 23
 };
 
 struct DqSmem {
@@ -101,15 +102,6 @@ __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// Plain (untiled) bulk copy global -> shared, completion on an mbarrier; 16-B aligned, size % 16 == 0.
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // 32 values as bf16 into chunks 4c .. 4c+3 of row r of a 128-byte-swizzled tile (row base `row`).
 __device__ __forceinline__ void store_chunk32(uint8_t* row, int c, int r, const float (&v)[32]) {
 #pragma unroll
@@ -153,11 +145,11 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       mbar_init(&bar[kSFree + i], 8);
       mbar_init(&bar[kDpFull + i], 1);
       mbar_init(&bar[kDpFree + i], 8);
-      mbar_init(&bar[kPFull + i], 8);
-      mbar_init(&bar[kPFree + i], 1);
-      mbar_init(&bar[kDsFull + i], 8);
-      mbar_init(&bar[kDsFree + i], 2);
     }
+    mbar_init(&bar[kPFull], 8);
+    mbar_init(&bar[kPFree], 1);
+    mbar_init(&bar[kDsFull], 8);
+    mbar_init(&bar[kDsFree], 2);
     mbar_init(&bar[kAccFull], 1);
     mbar_init(&bar[kKvDrain], 1);
     *abort_flag = 0;
@@ -201,15 +193,13 @@ __global__ void __launch_bounds__(kKvThreads, 1)
         }
         const int q0 = (t0 + t) * kSub;
         uint64_t* fb = &bar[kQFull + st];
-        mbar_arrive_expect_tx(fb, 2 * kQTile + 2 * kSub * 4);
+        mbar_arrive_expect_tx(fb, 2 * kQTile);
         uint8_t* sq = smem + KvSmem::Q + st * kQTile;
         uint8_t* sd = smem + KvSmem::DO + st * kQTile;
         tma_load_2d(sq, &tm_q, fb, qc, tok0 + q0);
         tma_load_2d(sq + kQAtom, &tm_q, fb, qc + 64, tok0 + q0);
         tma_load_2d(sd, &tm_do, fb, h * kHd, tok0 + q0);
         tma_load_2d(sd + kQAtom, &tm_do, fb, h * kHd + 64, tok0 + q0);
-        bulk_load(smem + KvSmem::L + st * kSub * 4, lse2 + stat0 + q0, kSub * 4, fb);
-        bulk_load(smem + KvSmem::DV + st * kSub * 4, rowsum + stat0 + q0, kSub * 4, fb);
         issued = t + 1;
       }
       if (*abort_flag) {  // let copies still in flight land before the CTA exits
@@ -257,34 +247,33 @@ __global__ void __launch_bounds__(kKvThreads, 1)
           ok = false;
           break;
         }
-        const int st = t & 1, qs = t % kQStages;
-        const uint32_t ph = (t >> 1) & 1;
+        const int qs = t % kQStages;
         const uint32_t sq = smem_u32(smem + KvSmem::Q + qs * kQTile);
         const uint32_t sd = smem_u32(smem + KvSmem::DO + qs * kQTile);
         // dV += P^T dO: P^T K-major over the 64 queries, dO hd-contiguous (two 64-wide blocks 8 KB apart)
-        if (!mbar_wait(&bar[kPFull + st], ph) || *abort_flag) {
+        if (!mbar_wait(&bar[kPFull], t & 1) || *abort_flag) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sp = smem_u32(smem + KvSmem::P + st * kPTile);
+        const uint32_t sp = smem_u32(smem + KvSmem::P);
 #pragma unroll
         for (int kk = 0; kk < kSub / 16; ++kk)
           umma_bf16(tmem + kColDv, smem_desc_sw128(sp + kk * 32, 16, 1024), smem_desc_sw128(sd + kk * 2048, kQAtom, 1024),
                     idesc_a, (t | kk) != 0 ? 1u : 0u);
-        umma_commit(&bar[kPFree + st]);
+        umma_commit(&bar[kPFree]);
         // dK += dS^T Q
-        if (!mbar_wait(&bar[kDsFull + st], ph) || *abort_flag) {
+        if (!mbar_wait(&bar[kDsFull], t & 1) || *abort_flag) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sds = smem_u32(smem + KvSmem::DS + st * kPTile);
+        const uint32_t sds = smem_u32(smem + KvSmem::DS);
 #pragma unroll
         for (int kk = 0; kk < kSub / 16; ++kk)
           umma_bf16(tmem + kColDk, smem_desc_sw128(sds + kk * 32, 16, 1024),
                     smem_desc_sw128(sq + kk * 2048, kQAtom, 1024), idesc_a, (t | kk) != 0 ? 1u : 0u);
-        umma_commit(&bar[kDsFree + st]);
+        umma_commit(&bar[kDsFree]);
         umma_commit(&bar[kQEmpty + qs]);
       }
       if (!ok) {
@@ -302,13 +291,12 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       // scratch row of (sequence-head bh, key block j, sub-block i): ((bh * nkb + j) * nsub + i) * 128
       int t = 0;
       for (; t < n; ++t) {
-        const int st = t & 1;
-        if (!mbar_wait(&bar[kDsFull + st], (t >> 1) & 1) || *abort_flag) break;
+        if (!mbar_wait(&bar[kDsFull], t & 1) || *abort_flag) break;
         const int row = ((bh * nkb + j) * nsub + t0 + t) * kKeys;
-        tma_store_2d(&tm_ds, smem + KvSmem::DS + st * kPTile, 0, row);
+        tma_store_2d(&tm_ds, smem + KvSmem::DS, 0, row);
         bulk_commit();
         bulk_wait_read_all();
-        mbar_arrive(&bar[kDsFree + st]);
+        mbar_arrive(&bar[kDsFree]);
       }
       if (t < n) {
         set_error(err, kDevTimeoutEpilogue);
@@ -323,8 +311,6 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     const int r = qw * 32 + lane;       // key row within the block
     const int kpos = k0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
-    const float* sl = reinterpret_cast<const float*>(smem + KvSmem::L);
-    const float* sdv = reinterpret_cast<const float*>(smem + KvSmem::DV);
     bool ok = true;
     auto wait = [&](uint64_t* bb, uint32_t parity) {
       bool w = ok && !*abort_flag && mbar_wait(bb, parity);
@@ -339,6 +325,8 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       const int st = t & 1, qs = t % kQStages;
       const uint32_t ph = (t >> 1) & 1;
       const int q0 = (t0 + t) * kSub + hh * 32;  // first query of this thread's 32 columns
+      // lse2 and rowsum of this warp's 32 queries: lane e holds query q0 + e (read from L2, shared by shuffles)
+      const float l_lane = __ldg(lse2 + stat0 + q0 + lane), d_lane = __ldg(rowsum + stat0 + q0 + lane);
       if (!wait(&bar[kQFull + qs], (t / kQStages) & 1) || !wait(&bar[kSFull + st], ph)) break;
       tc_fence_after();
       uint32_t v[32];
@@ -347,16 +335,15 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kSFree + st]);
-      const float* L = sl + qs * kSub + hh * 32;
       float p[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
-        const float pe = exp2f(__uint_as_float(v[e]) * scale_log2 - L[e]);
+        const float pe = exp2f(__uint_as_float(v[e]) * scale_log2 - __shfl_sync(0xffffffffu, l_lane, e));
         p[e] = q0 + e >= kpos ? pe : 0.f;  // causal: query before key -> 0
       }
       // P^T row r, columns 32 hh .. +31: 4 chunks of 16 B, chunk c at (c ^ r % 8) * 16
-      if (!wait(&bar[kPFree + st], ph ^ 1)) break;
-      uint8_t* prow = smem + KvSmem::P + st * kPTile + r * 128;
+      if (!wait(&bar[kPFree], (t & 1) ^ 1)) break;
+      uint8_t* prow = smem + KvSmem::P + r * 128;
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         *reinterpret_cast<uint4*>(prow + (((hh * 4 + u) ^ (r & 7)) << 4)) =
@@ -364,7 +351,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
                        pack_bf16x2(p[8 * u + 4], p[8 * u + 5]), pack_bf16x2(p[8 * u + 6], p[8 * u + 7]));
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kPFull + st]);
+      if (lane == 0) mbar_arrive(&bar[kPFull]);
       if (!wait(&bar[kDpFull + st], ph)) break;
       tc_fence_after();
       tmem_ld32(tmem + kColDp + st * kSub + lane_off + hh * 32, v);
@@ -372,11 +359,10 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kDpFree + st]);
-      const float* Dd = sdv + qs * kSub + hh * 32;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) p[e] = p[e] * (__uint_as_float(v[e]) - Dd[e]);
-      if (!wait(&bar[kDsFree + st], ph ^ 1)) break;
-      uint8_t* drow = smem + KvSmem::DS + st * kPTile + r * 128;
+      for (int e = 0; e < 32; ++e) p[e] = p[e] * (__uint_as_float(v[e]) - __shfl_sync(0xffffffffu, d_lane, e));
+      if (!wait(&bar[kDsFree], (t & 1) ^ 1)) break;
+      uint8_t* drow = smem + KvSmem::DS + r * 128;
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         *reinterpret_cast<uint4*>(drow + (((hh * 4 + u) ^ (r & 7)) << 4)) =
@@ -384,7 +370,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
                        pack_bf16x2(p[8 * u + 4], p[8 * u + 5]), pack_bf16x2(p[8 * u + 6], p[8 * u + 7]));
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kDsFull + st]);
+      if (lane == 0) mbar_arrive(&bar[kDsFull]);
     }
     // RoPE tables of this key position for head-dim pairs [32 hh, 32 hh + 32), loaded
     // while the last MMAs run

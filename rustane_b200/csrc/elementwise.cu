@@ -78,6 +78,37 @@ __global__ void embed_scatter_kernel(const float* __restrict__ dx, const int32_t
 }
 
 // --------------------------------------------------------------- RMSNorm
+// One warp per token row (cpu/rmsnorm.rs:149-183): the row's NV float4 per lane
+// are loaded once into registers (all loads in flight together), reduced, then
+// scaled and written; NV = D / 128.  Generic widths re-read the row.
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_reg_kernel(const float* __restrict__ x,
+                                                              const float* __restrict__ gamma,
+                                                              __nv_bfloat16* __restrict__ out,
+                                                              float* __restrict__ rms_inv, int M, int D) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(row) * D);
+  float4 v[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) v[k] = xr[lane + 32 * k];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(D)) + kRmsEps);
+  if (lane == 0) rms_inv[row] = r;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * D);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int c = lane + 32 * k;
+    const float4 g = __ldg(g4 + c);
+    o[c] = make_uint2(pack_bf16x2(v[k].x * r * g.x, v[k].y * r * g.y), pack_bf16x2(v[k].z * r * g.z, v[k].w * r * g.w));
+  }
+}
+
 __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                    __nv_bfloat16* __restrict__ out, float* __restrict__ rms_inv, int M, int D) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -186,7 +217,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // of 4 rows (g = blockIdx.x, + gridDim.x, ...); the dy and x rows of the next
 // STAGES - 1 groups stream into shared memory with cp.async while the current
 // group is computed, so HBM stays busy without holding rows in registers (the
-// residual-gradient row is loaded into registers at the start of its group).  Warps 2r and 2r+1 own the two halves of row r of a group.  Each
+// residual-gradient row is loaded into registers one group ahead).  Warps 2r and 2r+1 own the two halves of row r of a group.  Each
 // thread sums dgamma for its columns over the rows it handles (its CTA's groups
 // in order); the CTA adds its four row slots in order into partial row
 // blockIdx.x: deterministic.
@@ -227,8 +258,22 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
   for (int st = 0; st < STAGES - 1; ++st) issue(blockIdx.x + st * gridDim.x, st);
   const float inv_d = 1.0f / static_cast<float>(D);
+  // residual gradient of this thread's columns: loaded one group ahead, in registers
+  float4 q[NV2], qn[NV2];
+  auto load_resid = [&](int grp, float4 (&dst)[NV2]) {
+    const int rw = grp * kGroupRows + r;
+    if (resid && grp < ngroups && rw < M) {
+      const float4* rs = reinterpret_cast<const float4*>(resid + static_cast<int64_t>(rw) * D);
+#pragma unroll
+      for (int k = 0; k < NV2; ++k) dst[k] = __ldcs(rs + h * (D4 / 2) + lane + 32 * k);
+    }
+  };
+  load_resid(blockIdx.x, qn);
   int it = 0;
   for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
+#pragma unroll
+    for (int k = 0; k < NV2; ++k) q[k] = qn[k];
+    load_resid(g + gridDim.x, qn);
     issue(g + (STAGES - 1) * gridDim.x, (it + STAGES - 1) % STAGES);
     cp_async_wait<STAGES - 1>();
     __syncthreads();  // every thread's copies of group g have landed
@@ -237,12 +282,6 @@ __global__ void __launch_bounds__(256, 1)
     const float4* sdy = sm + (stage * 2 + 0) * kGroupRows * D4 + r * D4;
     const float4* sx = sm + (stage * 2 + 1) * kGroupRows * D4 + r * D4;
     const float rinv = row < M ? rms_inv[row] : 0.f;
-    float4 q[NV2];  // residual gradient of this thread's columns, in flight during the dot product
-    if (resid && row < M) {
-      const float4* rs = reinterpret_cast<const float4*>(resid + static_cast<int64_t>(row) * D);
-#pragma unroll
-      for (int k = 0; k < NV2; ++k) q[k] = rs[h * (D4 / 2) + lane + 32 * k];
-    }
     if (row < M) {
       float dot = 0.f;
 #pragma unroll
@@ -310,15 +349,26 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 // dgamma[d] = (accumulate ? dgamma[d] : 0) + sum_b part[b][d]: 32 columns per block,
-// warp w sums partials w, w+8, ... in order, then the 8 warp sums in order.
+// warp w sums partials w, w+8, ... in order (loads unrolled by 4, all in flight),
+// then the 8 warp sums in order.
 __global__ void __launch_bounds__(256) dgamma_reduce_kernel(const float* __restrict__ part, int nblk,
                                                             float* __restrict__ dgamma, int D, int accumulate) {
   __shared__ float red[8][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int d = blockIdx.x * 32 + lane;
   float s = 0.f;
-  if (d < D)
-    for (int b = warp; b < nblk; b += 8) s += part[static_cast<int64_t>(b) * D + d];
+  if (d < D) {
+    int b = warp;
+    for (; b + 24 < nblk; b += 32) {
+      const float a0 = part[static_cast<int64_t>(b) * D + d], a1 = part[static_cast<int64_t>(b + 8) * D + d];
+      const float a2 = part[static_cast<int64_t>(b + 16) * D + d], a3 = part[static_cast<int64_t>(b + 24) * D + d];
+      s += a0;
+      s += a1;
+      s += a2;
+      s += a3;
+    }
+    for (; b < nblk; b += 8) s += part[static_cast<int64_t>(b) * D + d];
+  }
   red[warp][lane] = s;
   __syncthreads();
   if (warp == 0 && d < D) {
@@ -645,7 +695,18 @@ int embed_scatter(const float* dx, const int32_t* perm, const int32_t* seg_start
 }
 int rmsnorm_fwd(const float* x, const float* gamma, __nv_bfloat16* out, float* rms_inv, int M, int D, cudaStream_t s) {
   if (D % 4) return -1;
-  rmsnorm_fwd_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, gamma, out, rms_inv, M, D);
+  const int grid = (M * 32 + 255) / 256;
+  switch (D % 128 == 0 ? D / 128 : 0) {
+    case 6: rmsnorm_fwd_reg_kernel<6><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    case 8: rmsnorm_fwd_reg_kernel<8><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    case 10: rmsnorm_fwd_reg_kernel<10><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    case 12: rmsnorm_fwd_reg_kernel<12><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    case 14: rmsnorm_fwd_reg_kernel<14><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    case 16: rmsnorm_fwd_reg_kernel<16><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    case 18: rmsnorm_fwd_reg_kernel<18><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    case 20: rmsnorm_fwd_reg_kernel<20><<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+    default: rmsnorm_fwd_kernel<<<grid, 256, 0, s>>>(x, gamma, out, rms_inv, M, D); break;
+  }
   return cudaGetLastError();
 }
 int rmsnorm_bwd_blocks(int M) { return norm_ctas(M); }

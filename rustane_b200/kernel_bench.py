@@ -2,7 +2,7 @@
 
     python -m rustane_b200.kernel_bench gemm --m 4096 --n 4096 --k 1536 --b-mn --epi swiglu [--bn -256 | --cublas]
     python -m rustane_b200.kernel_bench attention --batch 8 --seq 512 --heads 12 [--bwd [--impl tc|mma]]
-    python -m rustane_b200.kernel_bench rmsnorm_bwd --m 4096 --d 1536
+    python -m rustane_b200.kernel_bench rmsnorm_bwd --m 4096 --d 1536   (or rmsnorm_fwd)
 
 Prints one JSON line (mean us per launch, TFLOP/s or GB/s).  Buffers come from
 torch; the kernels run through librustane_cuda.so's rt_kernel_* entry points.
@@ -133,9 +133,24 @@ def bench_rmsnorm_bwd(args):
     return {"kernel": "rmsnorm_bwd", "M": M, "D": D, "us": us, "gbs": bytes_ / us / 1e3}
 
 
+def bench_rmsnorm_fwd(args):
+    import torch
+    L = _lib.lib()
+    M, D = args.m, args.d
+    x = torch.randn(M, D, device="cuda")
+    g = torch.ones(D, device="cuda")
+    r = torch.empty(M, device="cuda")
+    out = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    st = torch.cuda.current_stream().cuda_stream
+    run = lambda: L.rt_kernel_rmsnorm_fwd(x.data_ptr(), g.data_ptr(), out.data_ptr(), r.data_ptr(), M, D, st)  # noqa
+    us = _time(run, args.iters)
+    bytes_ = M * D * (4 + 2)  # read x (fp32), write the bf16 output
+    return {"kernel": "rmsnorm_fwd", "M": M, "D": D, "us": us, "gbs": bytes_ / us / 1e3}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "rmsnorm_bwd"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "rmsnorm_bwd", "rmsnorm_fwd"])
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=1536)
@@ -153,7 +168,8 @@ def main():
     ap.add_argument("--impl", default="tc", choices=["tc", "mma"], help="attention backward kernels")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
-    fn = {"gemm": bench_gemm, "attention": bench_attention, "rmsnorm_bwd": bench_rmsnorm_bwd}[args.kernel]
+    fn = {"gemm": bench_gemm, "attention": bench_attention, "rmsnorm_bwd": bench_rmsnorm_bwd,
+          "rmsnorm_fwd": bench_rmsnorm_fwd}[args.kernel]
     print(json.dumps(fn(args)), flush=True)
 
 

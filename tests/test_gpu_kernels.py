@@ -75,11 +75,12 @@ def test_embed_scatter_bit_exact():  # cpu/embedding.rs:34-44 order: ascending p
 
 
 # --------------------------------------------------------------- RMSNorm
-# D <= 2048 and a multiple of 128 take the fused backward (dgamma partials in the
-# same pass), other widths the row + column-partial kernels; M = 101 leaves a
-# partial last block of rows
+# Backward: D a multiple of 256 up to 2048 takes the pipelined kernel (dgamma partials
+# in the same pass), other widths the row + column-partial kernels.  Forward: D a
+# multiple of 128 from 768 to 2560 keeps the row in registers, other widths re-read
+# it (256, 1000).  M = 101 leaves a partial last block of rows.
 @pytest.mark.parametrize("M", [96, 101])
-@pytest.mark.parametrize("D", [256, 1536, 2048, 2560])
+@pytest.mark.parametrize("D", [256, 768, 1000, 1280, 1536, 2048, 2560])
 def test_rmsnorm_fwd_bwd_vs_oracle(D, M):
     rng = np.random.default_rng(D)
     x = rng.standard_normal((M, D)).astype(np.float32)
