@@ -475,6 +475,7 @@ __global__ void mean_reduce_kernel(const float* __restrict__ x, int n, float* __
 // ---------------------------------------------------------- grad norm
 constexpr int kNormBlocks = 1024;
 constexpr int kNormThreads = 256;
+constexpr int kSegNormBlocks = 148;  // partials per gradient segment of the train step (one per SM)
 
 __global__ void __launch_bounds__(kNormThreads) sumsq_partial_kernel(const float* __restrict__ x, int64_t n,
                                                                       float* __restrict__ partials) {
@@ -768,6 +769,16 @@ int mean_reduce(const float* row_loss, int M, float* out, cudaStream_t s) {
   return cudaGetLastError();
 }
 int sumsq_partials_count() { return kNormBlocks; }
+int sumsq_seg_blocks() { return kSegNormBlocks; }
+int sumsq_partials(const float* x, int64_t n, float* partials, cudaStream_t s) {
+  if (reinterpret_cast<uintptr_t>(x) & 15) return -1;
+  sumsq_partial_kernel<<<kSegNormBlocks, kNormThreads, 0, s>>>(x, n, partials);
+  return cudaGetLastError();
+}
+int sumsq_finish(const float* partials, int n, float* out_norm, cudaStream_t s) {
+  sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, n, out_norm);
+  return cudaGetLastError();
+}
 int sumsq_norm(const float* x, int64_t n, float* partials, float* out_norm, cudaStream_t s) {
   sumsq_partial_kernel<<<kNormBlocks, kNormThreads, 0, s>>>(x, n, partials);
   sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, kNormBlocks, out_norm);

@@ -42,6 +42,12 @@ int mean_reduce(const float* row_loss, int M, float* out, cudaStream_t s);
 // Global L2 norm over n fp32 values: partials then a fixed-order final pass.
 int sumsq_norm(const float* x, int64_t n, float* partials, float* out_norm, cudaStream_t s);
 int sumsq_partials_count();
+// Segmented form: sumsq_partials writes sumsq_seg_blocks() partial sums of squares of
+// x[0, n) (x 16-byte aligned); sumsq_finish reduces n partials in a fixed order to the
+// L2 norm.  The train step reduces each layer's gradients as soon as they are final.
+int sumsq_seg_blocks();
+int sumsq_partials(const float* x, int64_t n, float* partials, cudaStream_t s);
+int sumsq_finish(const float* partials, int n, float* out_norm, cudaStream_t s);
 
 // Multi-tensor AdamW over up to 4 contiguous segments of one parameter arena
 // (crates/engine/src/cpu/adam.rs:95-132 per element).  The gradient scale is

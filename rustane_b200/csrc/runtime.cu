@@ -195,6 +195,11 @@ int other(rt_ctx* c, int nk, int rc_in, const char* what) {
     int _r = launch(c, 2, 0.0, nk, [&] { return (expr); }); \
     if (_r != 0) return other(c, nk, _r, what); \
   } while (0)
+#define RT_OTHER_ON(st, nk, expr, what) \
+  do {                                  \
+    int _r = launch_on(c, st, 2, 0.0, nk, [&] { return (expr); }); \
+    if (_r != 0) return other(c, nk, _r, what); \
+  } while (0)
 
 bool forward_only(const rt_ctx* c) { return (c->flags & RT_CTX_FORWARD_ONLY) != 0; }
 float alpha_of(const rt_model_config& cfg) { return 1.0f / std::sqrt(2.0f * static_cast<float>(cfg.nlayers)); }
@@ -759,14 +764,24 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + c->off_gamma_final, D, beta, ms), "dgamma");
   float* dy = c->dy_a;
   float* dy_next = c->dy_b;
+  // Gradient segments that are final go to the comm stream: all-reduced (data
+  // parallel) and / or reduced to grad-norm partials (train step), while the
+  // backward continues.  Partials: [embed | layer 0 .. L-1 | gammas], SB each.
+  const bool seg_norm = c->layer_sumsq;
+  const int SB = rt::sumsq_seg_blocks();
   for (int l = L - 1; l >= 0; --l) {
     if ((rc = layer_backward(c, l, dy, dy_next, beta))) return rc;
     const auto& o = c->layer_off[l];
+    if (c->overlap_allreduce || seg_norm) cudaStreamWaitEvent(c->s_comm, c->ev_dw_done[l], 0);
     if (c->overlap_allreduce) {  // this layer's matrices are final: reduce them while backward continues
-      cudaStreamWaitEvent(c->s_comm, c->ev_dw_done[l], 0);
       if (l == L - 1) cudaEventRecord(c->ev[4], c->s_comm);
       if ((rc = allreduce_range(c, o.wqkv, o.w2 + int64_t(D) * H, c->s_comm))) return rc;
     }
+    if (seg_norm)
+      RT_OTHER_ON(c->s_comm, 1,
+                  rt::sumsq_partials(Gr + o.wqkv, o.w2 + int64_t(D) * H - o.wqkv, c->norm_partials + (1 + l) * SB,
+                                     c->s_comm),
+                  "grad norm");
     std::swap(dy, dy_next);
   }
   // embedding scatter-add (full_model.rs:330), after the dE GEMM
@@ -774,13 +789,22 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   RT_OTHER(1, rt::embed_scatter(dy, c->cur->perm, c->cur->seg_start, c->cur->seg_tok, c->cur->nseg, Gr, D, ms),
            "embed scatter");
   cudaStreamWaitEvent(ms, c->ev_dw_done[0], 0);  // every weight gradient is final
-  if (c->overlap_allreduce) {  // last buckets: embedding and the gammas
+  if (c->overlap_allreduce || seg_norm) {  // last segments: embedding and the gammas
     cudaEventRecord(c->ev_main_done, ms);
     cudaStreamWaitEvent(c->s_comm, c->ev_main_done, 0);
-    if ((rc = allreduce_range(c, 0, c->n_embed, c->s_comm))) return rc;
-    if ((rc = allreduce_range(c, c->n_matrix_end, c->n_params, c->s_comm))) return rc;
-    cudaEventRecord(c->ev[5], c->s_comm);
-    c->ev_recorded |= 4u;
+    if (c->overlap_allreduce) {
+      if ((rc = allreduce_range(c, 0, c->n_embed, c->s_comm))) return rc;
+      if ((rc = allreduce_range(c, c->n_matrix_end, c->n_params, c->s_comm))) return rc;
+      cudaEventRecord(c->ev[5], c->s_comm);
+      c->ev_recorded |= 4u;
+    }
+    if (seg_norm) {
+      RT_OTHER_ON(c->s_comm, 1, rt::sumsq_partials(Gr, c->n_embed, c->norm_partials, c->s_comm), "grad norm");
+      RT_OTHER_ON(c->s_comm, 1,
+                  rt::sumsq_partials(Gr + c->n_matrix_end, c->n_params - c->n_matrix_end,
+                                     c->norm_partials + int64_t(L + 1) * SB, c->s_comm),
+                  "grad norm");
+    }
     cudaEventRecord(c->ev_comm_all, c->s_comm);
     cudaStreamWaitEvent(ms, c->ev_comm_all, 0);
   }
@@ -961,7 +985,8 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
   c->row_lse = dalloc<float>(c, M);
   c->d_loss = dalloc<float>(c, 4);
   c->d_norm = dalloc<float>(c, 4);
-  c->norm_partials = dalloc<float>(c, rt::sumsq_partials_count());
+  c->norm_partials = dalloc<float>(
+      c, std::max<int64_t>(rt::sumsq_partials_count(), int64_t(cfg.nlayers + 2) * rt::sumsq_seg_blocks()));
   c->dy_a = dalloc<float>(c, M * D);
   for (void* p : {(void*)c->x_out, (void*)c->xf, (void*)c->rms_f, (void*)c->logits, (void*)c->row_loss,
                   (void*)c->row_lse, (void*)c->d_loss, (void*)c->d_norm, (void*)c->norm_partials, (void*)c->dy_a})
@@ -1436,11 +1461,14 @@ static int train_step_device(rt_ctx* c, const rt::TokenBatch& tb, uint32_t step,
   if ((rc = forward_impl(c, batch, tc->softcap))) return rc;
   // data parallel: gradients are all-reduced bucket by bucket inside the backward
   c->overlap_allreduce = c->world > 1 && c->dist_mode == RT_DIST_DATA_PARALLEL;
+  c->layer_sumsq = true;  // grad-norm partials of each segment as soon as it is final
   rc = backward_impl(c, tc->softcap, tc->loss_scale);
   c->overlap_allreduce = false;
+  c->layer_sumsq = false;
   if (rc) return rc;
   cudaEventRecord(c->ev[6], c->stream);
-  RT_OTHER(2, rt::sumsq_norm(c->grads, c->n_params, c->norm_partials, c->d_norm, c->stream), "grad norm");
+  RT_OTHER(1, rt::sumsq_finish(c->norm_partials, (c->cfg.nlayers + 2) * rt::sumsq_seg_blocks(), c->d_norm, c->stream),
+           "grad norm");
   const float gsc = 1.0f / (static_cast<float>(batch) * static_cast<float>(c->world) * tc->loss_scale);
   const float lr = rt_learning_rate(step, tc);
   if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip))) return rc;

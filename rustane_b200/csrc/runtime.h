@@ -152,6 +152,7 @@ struct rt_ctx {
   std::vector<cudaEvent_t> ev_dgate, ev_rms2, ev_attn, ev_dw_done, ev_comm;
   cudaEvent_t ev_ce = nullptr, ev_de = nullptr, ev_main_done = nullptr, ev_comm_all = nullptr;
   bool overlap_allreduce = false;  // set by the train step of a data-parallel context
+  bool layer_sumsq = false;        // set by the train step: grad-norm partials per final gradient segment
 
   // timing
   cudaEvent_t ev[8] = {};
