@@ -61,7 +61,7 @@ extern "C" {
 #define RT_CTX_FORWARD_ONLY 1 /* bf16 weights only, activations reused layer to layer        */
 
 /* rt_dist_init modes */
-#define RT_DIST_DATA_PARALLEL 0   /* gradients all-reduced (sum) before grad-norm / AdamW */
+#define RT_DIST_DATA_PARALLEL 0   /* gradients summed over ranks before grad-norm / AdamW (sharded AdamW) */
 #define RT_DIST_TENSOR_PARALLEL 1 /* forward-only: heads / hidden sharded, all-reduce after Wo and W2 */
 
 /* ----------------------------------------------------------------- types */
@@ -250,7 +250,18 @@ RT_API int rt_checkpoint_read(const char* path, const rt_model_config* cfg, uint
 RT_API int rt_nccl_unique_id(uint8_t* out128);
 /* Join a communicator of `world` ranks (one process per GPU).  mode:
  * RT_DIST_DATA_PARALLEL or RT_DIST_TENSOR_PARALLEL.  Collectives that do not
- * finish within timeout_ms abort the communicator and return RT_ERR_NCCL. */
+ * finish within timeout_ms abort the communicator and return RT_ERR_NCCL.
+ * Data parallel: rt_train_step reduce-scatters each gradient segment (the
+ * embedding, each layer's matrices, the gammas) as soon as the backward has
+ * finished it, every rank runs AdamW on its 1/world chunk of every segment
+ * (the grad norm is summed over the ranks first), and the weights the forward
+ * reads are all-gathered -- the same update as an all-reduce of the gradients
+ * followed by AdamW on every rank.  The fp32 matrices, the AdamW moments and the
+ * gradients then stay sharded; rt_weights_download, rt_opt_download,
+ * rt_grads_download, rt_grad_norm, rt_clip_grads, rt_update_weights and an
+ * accumulating rt_backward gather them first, so every rank must make those
+ * calls together.  When a segment does not split into 16-byte chunks per rank
+ * (or RUSTANE_DP_ALLREDUCE=1 is set), the gradients are all-reduced instead. */
 RT_API int rt_dist_init(rt_ctx* ctx, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms);
 /* Sum the gradients over the data-parallel ranks (one in-place all-reduce). */
 RT_API int rt_grad_allreduce(rt_ctx* ctx);

@@ -504,7 +504,10 @@ __global__ void __launch_bounds__(kNormThreads) sumsq_partial_kernel(const float
   }
 }
 
-__global__ void sumsq_final_kernel(const float* __restrict__ partials, int n, float* __restrict__ out) {
+// Sum of the partials in a fixed order (double): out_norm = sqrt(sum) as float, or
+// out_sq = sum when out_norm is null.
+__global__ void sumsq_final_kernel(const float* __restrict__ partials, int n, float* __restrict__ out,
+                                   double* __restrict__ out_sq) {
   __shared__ double red[32];
   double s = 0.0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) s += partials[i];
@@ -517,13 +520,20 @@ __global__ void sumsq_final_kernel(const float* __restrict__ partials, int n, fl
     double r = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
 #pragma unroll
     for (int o = 16; o; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-    if (lane == 0) out[0] = static_cast<float>(sqrt(r));
+    if (lane == 0) {
+      if (out) out[0] = static_cast<float>(sqrt(r));
+      if (out_sq) out_sq[0] = r;
+    }
   }
+}
+
+__global__ void sqrt_to_float_kernel(const double* __restrict__ sq, float* __restrict__ out) {
+  out[0] = static_cast<float>(sqrt(sq[0]));
 }
 
 // ----------------------------------------------------------------- AdamW
 struct AdamKParams {
-  AdamSegment seg[4];
+  AdamSegment seg[kMaxAdamSegments];
   int nseg;
   float beta1, beta2, eps, bc1, bc2, grad_scale, gsc, clip;
 };
@@ -776,17 +786,26 @@ int sumsq_partials(const float* x, int64_t n, float* partials, cudaStream_t s) {
   return cudaGetLastError();
 }
 int sumsq_finish(const float* partials, int n, float* out_norm, cudaStream_t s) {
-  sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, n, out_norm);
+  sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, n, out_norm, nullptr);
+  return cudaGetLastError();
+}
+int sumsq_finish_sq(const float* partials, int n, double* out_sq, cudaStream_t s) {
+  sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, n, nullptr, out_sq);
+  return cudaGetLastError();
+}
+int sqrt_to_float(const double* sq, float* out, cudaStream_t s) {
+  sqrt_to_float_kernel<<<1, 1, 0, s>>>(sq, out);
   return cudaGetLastError();
 }
 int sumsq_norm(const float* x, int64_t n, float* partials, float* out_norm, cudaStream_t s) {
   sumsq_partial_kernel<<<kNormBlocks, kNormThreads, 0, s>>>(x, n, partials);
-  sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, kNormBlocks, out_norm);
+  sumsq_final_kernel<<<1, 1024, 0, s>>>(partials, kNormBlocks, out_norm, nullptr);
   return cudaGetLastError();
 }
 int adam_step(const AdamArgs& a, cudaStream_t s) {
   AdamKParams k;
-  for (int i = 0; i < 4; ++i) k.seg[i] = a.seg[i];
+  if (a.nseg < 0 || a.nseg > kMaxAdamSegments) return -1;
+  for (int i = 0; i < a.nseg; ++i) k.seg[i] = a.seg[i];
   k.nseg = a.nseg;
   int64_t total = 0;
   for (int i = 0; i < a.nseg; ++i) {

@@ -48,11 +48,16 @@ int sumsq_partials_count();
 int sumsq_seg_blocks();
 int sumsq_partials(const float* x, int64_t n, float* partials, cudaStream_t s);
 int sumsq_finish(const float* partials, int n, float* out_norm, cudaStream_t s);
+// The same reduction without the square root, in double (for a cross-rank sum),
+// and the square root of that sum into a float.
+int sumsq_finish_sq(const float* partials, int n, double* out_sq, cudaStream_t s);
+int sqrt_to_float(const double* sq, float* out, cudaStream_t s);
 
 // Multi-tensor AdamW over up to 4 contiguous segments of one parameter arena
 // (crates/engine/src/cpu/adam.rs:95-132 per element).  The gradient scale is
 // either `grad_scale` or, when `norm` is non-null, the train-step clip rule
 // (full_model.rs:696-704): raw = *norm; scale = raw*gsc > clip ? clip/raw : gsc.
+constexpr int kMaxAdamSegments = 72;  // 3 learning-rate groups, or one chunk per gradient segment (sharded)
 struct AdamSegment {
   int64_t begin = 0, end = 0;  // element range in the arena
   float lr = 0.f, wd = 0.f;
@@ -64,7 +69,7 @@ struct AdamArgs {
   float* m = nullptr;
   float* v = nullptr;
   __nv_bfloat16* param_bf16 = nullptr;
-  AdamSegment seg[4];
+  AdamSegment seg[kMaxAdamSegments];
   int nseg = 0;
   float beta1 = 0.9f, beta2 = 0.95f, eps = 1e-8f, bc1 = 1.f, bc2 = 1.f;
   float grad_scale = 1.f;

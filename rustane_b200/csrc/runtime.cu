@@ -33,6 +33,10 @@ struct NcclApi {
   decltype(&ncclGetUniqueId) getUniqueId = nullptr;
   decltype(&ncclCommInitRank) commInitRank = nullptr;
   decltype(&ncclAllReduce) allReduce = nullptr;
+  decltype(&ncclReduceScatter) reduceScatter = nullptr;
+  decltype(&ncclAllGather) allGather = nullptr;
+  decltype(&ncclGroupStart) groupStart = nullptr;
+  decltype(&ncclGroupEnd) groupEnd = nullptr;
   decltype(&ncclCommGetAsyncError) getAsyncError = nullptr;
   decltype(&ncclCommAbort) commAbort = nullptr;
   decltype(&ncclCommDestroy) commDestroy = nullptr;
@@ -59,6 +63,10 @@ static NcclApi* nccl_api() {
   RT_SYM(getUniqueId, "ncclGetUniqueId");
   RT_SYM(commInitRank, "ncclCommInitRank");
   RT_SYM(allReduce, "ncclAllReduce");
+  RT_SYM(reduceScatter, "ncclReduceScatter");
+  RT_SYM(allGather, "ncclAllGather");
+  RT_SYM(groupStart, "ncclGroupStart");
+  RT_SYM(groupEnd, "ncclGroupEnd");
   RT_SYM(getAsyncError, "ncclCommGetAsyncError");
   RT_SYM(commAbort, "ncclCommAbort");
   RT_SYM(commDestroy, "ncclCommDestroy");
@@ -347,6 +355,7 @@ int materialize_zero_grads(rt_ctx* c) {
   if (c->grads_zero_pending) {
     RT_CUDA(cudaMemsetAsync(c->grads, 0, sizeof(float) * c->n_params, c->stream), "zero grads");
     c->grads_zero_pending = false;
+    c->sharded_g = false;
   }
   return RT_OK;
 }
@@ -596,6 +605,73 @@ int allreduce_range(rt_ctx* c, int64_t begin, int64_t end, cudaStream_t st) {
   return RT_OK;
 }
 
+// ---- data-parallel sharding (see rt_ctx::zero)
+int64_t seg_chunk(const rt_ctx* c, int i) { return (c->segs[i].second - c->segs[i].first) / c->world; }
+int64_t seg_own(const rt_ctx* c, int i) { return c->segs[i].first + c->rank * seg_chunk(c, i); }
+
+int nccl_ok(rt_ctx* c, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return RT_OK;
+  return set_err(c, RT_ERR_NCCL, std::string(what) + ": " + rt::nccl_api()->errorString(r));
+}
+
+// Gradient segment i summed over the ranks into this rank's chunk (in place).
+int reduce_scatter_seg(rt_ctx* c, int i, cudaStream_t st) {
+  rt::NcclApi* api = rt::nccl_api();
+  if (!api || !c->nccl || !c->nccl->comm) return set_err(c, RT_ERR_NCCL, "no communicator (aborted or not initialised)");
+  float* base = c->grads + c->segs[i].first;
+  return nccl_ok(c, api->reduceScatter(base, c->grads + seg_own(c, i), static_cast<size_t>(seg_chunk(c, i)),
+                                       ncclFloat32, ncclSum, c->nccl->comm, st),
+                 "ncclReduceScatter");
+}
+
+// Every rank's chunk of segment i of `arena` (fp32, or the bf16 copy) to all ranks (in place).
+int gather_seg(rt_ctx* c, void* arena, bool bf16, int i, cudaStream_t st) {
+  rt::NcclApi* api = rt::nccl_api();
+  if (!api || !c->nccl || !c->nccl->comm) return set_err(c, RT_ERR_NCCL, "no communicator (aborted or not initialised)");
+  const size_t es = bf16 ? 2 : 4;
+  char* base = static_cast<char*>(arena) + c->segs[i].first * es;
+  char* own = static_cast<char*>(arena) + seg_own(c, i) * es;
+  return nccl_ok(c, api->allGather(own, base, static_cast<size_t>(seg_chunk(c, i)), bf16 ? ncclBfloat16 : ncclFloat32,
+                                   c->nccl->comm, st),
+                 "ncclAllGather");
+}
+
+// Gathers of several segments as one NCCL group.
+template <class F>
+int nccl_group(rt_ctx* c, F&& body) {
+  rt::NcclApi* api = rt::nccl_api();
+  if (api && api->groupStart) api->groupStart();
+  const int rc = body();
+  if (api && api->groupEnd) {
+    const ncclResult_t r = api->groupEnd();
+    if (rc == RT_OK && r != ncclSuccess) return nccl_ok(c, r, "ncclGroupEnd");
+  }
+  return rc;
+}
+
+// Collective: make the sharded arrays whole again on every rank (fp32 matrices
+// and embedding / gammas, moments, gradients) before a call that reads them.
+int zero_gather(rt_ctx* c, bool params, bool moments, bool grads) {
+  const int nseg = static_cast<int>(c->segs.size());
+  const bool gp = params && c->sharded_p, gm = moments && c->sharded_mv, gg = grads && c->sharded_g;
+  if (!gp && !gm && !gg) return RT_OK;
+  int rc = nccl_group(c, [&] {
+    int r = RT_OK;
+    for (int i = 0; i < nseg && r == RT_OK; ++i) {
+      if (gp && i > 0 && i + 1 < nseg) r = gather_seg(c, c->params, false, i, c->stream);  // matrices
+      if (r == RT_OK && gm) r = gather_seg(c, c->mom1, false, i, c->stream);
+      if (r == RT_OK && gm) r = gather_seg(c, c->mom2, false, i, c->stream);
+      if (r == RT_OK && gg) r = gather_seg(c, c->grads, false, i, c->stream);
+    }
+    return r;
+  });
+  if (rc) return rc;
+  if (gp) c->sharded_p = false;
+  if (gm) c->sharded_mv = false;
+  if (gg) c->sharded_g = false;
+  return RT_OK;
+}
+
 // Backward of the last forward.  The data-gradient chain (dlogits -> dx of each
 // layer) runs on the main stream; each layer's four weight-gradient GEMMs run on
 // s_dw as soon as their inputs exist, reading parity-double-buffered
@@ -773,15 +849,18 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
     if ((rc = layer_backward(c, l, dy, dy_next, beta))) return rc;
     const auto& o = c->layer_off[l];
     if (c->overlap_allreduce || seg_norm) cudaStreamWaitEvent(c->s_comm, c->ev_dw_done[l], 0);
+    const bool shard = c->overlap_allreduce && c->zero;
     if (c->overlap_allreduce) {  // this layer's matrices are final: reduce them while backward continues
       if (l == L - 1) cudaEventRecord(c->ev[4], c->s_comm);
-      if ((rc = allreduce_range(c, o.wqkv, o.w2 + int64_t(D) * H, c->s_comm))) return rc;
+      rc = shard ? reduce_scatter_seg(c, 1 + l, c->s_comm) : allreduce_range(c, o.wqkv, o.w2 + int64_t(D) * H, c->s_comm);
+      if (rc) return rc;
     }
-    if (seg_norm)
-      RT_OTHER_ON(c->s_comm, 1,
-                  rt::sumsq_partials(Gr + o.wqkv, o.w2 + int64_t(D) * H - o.wqkv, c->norm_partials + (1 + l) * SB,
-                                     c->s_comm),
+    if (seg_norm) {  // sharded: this rank's chunk only (the ranks' sums are added after the backward)
+      const int64_t b0 = shard ? seg_own(c, 1 + l) : o.wqkv;
+      const int64_t n = shard ? seg_chunk(c, 1 + l) : o.w2 + int64_t(D) * H - o.wqkv;
+      RT_OTHER_ON(c->s_comm, 1, rt::sumsq_partials(Gr + b0, n, c->norm_partials + (1 + l) * SB, c->s_comm),
                   "grad norm");
+    }
     std::swap(dy, dy_next);
   }
   // embedding scatter-add (full_model.rs:330), after the dE GEMM
@@ -792,17 +871,24 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   if (c->overlap_allreduce || seg_norm) {  // last segments: embedding and the gammas
     cudaEventRecord(c->ev_main_done, ms);
     cudaStreamWaitEvent(c->s_comm, c->ev_main_done, 0);
+    const bool shard = c->overlap_allreduce && c->zero;
     if (c->overlap_allreduce) {
-      if ((rc = allreduce_range(c, 0, c->n_embed, c->s_comm))) return rc;
-      if ((rc = allreduce_range(c, c->n_matrix_end, c->n_params, c->s_comm))) return rc;
+      if (shard) {
+        if ((rc = reduce_scatter_seg(c, 0, c->s_comm))) return rc;
+        if ((rc = reduce_scatter_seg(c, L + 1, c->s_comm))) return rc;
+      } else {
+        if ((rc = allreduce_range(c, 0, c->n_embed, c->s_comm))) return rc;
+        if ((rc = allreduce_range(c, c->n_matrix_end, c->n_params, c->s_comm))) return rc;
+      }
       cudaEventRecord(c->ev[5], c->s_comm);
       c->ev_recorded |= 4u;
     }
     if (seg_norm) {
-      RT_OTHER_ON(c->s_comm, 1, rt::sumsq_partials(Gr, c->n_embed, c->norm_partials, c->s_comm), "grad norm");
-      RT_OTHER_ON(c->s_comm, 1,
-                  rt::sumsq_partials(Gr + c->n_matrix_end, c->n_params - c->n_matrix_end,
-                                     c->norm_partials + int64_t(L + 1) * SB, c->s_comm),
+      const int64_t e0 = shard ? seg_own(c, 0) : 0, en = shard ? seg_chunk(c, 0) : c->n_embed;
+      const int64_t g0 = shard ? seg_own(c, L + 1) : c->n_matrix_end;
+      const int64_t gn = shard ? seg_chunk(c, L + 1) : c->n_params - c->n_matrix_end;
+      RT_OTHER_ON(c->s_comm, 1, rt::sumsq_partials(Gr + e0, en, c->norm_partials, c->s_comm), "grad norm");
+      RT_OTHER_ON(c->s_comm, 1, rt::sumsq_partials(Gr + g0, gn, c->norm_partials + int64_t(L + 1) * SB, c->s_comm),
                   "grad norm");
     }
     cudaEventRecord(c->ev_comm_all, c->s_comm);
@@ -821,17 +907,32 @@ float powi_f32(float b, uint32_t t) {
 }
 
 int adam_impl(rt_ctx* c, uint32_t t, float lr, const rt_train_config* tc, float grad_scale, const float* d_norm,
-              float gsc, float clip) {
+              float gsc, float clip, bool shard = false) {
   rt::AdamArgs a;
   a.param = c->params;
   a.grad = c->grads;
   a.m = c->mom1;
   a.v = c->mom2;
   a.param_bf16 = c->params_bf16;
-  a.nseg = 3;
-  a.seg[0] = {0, c->n_embed, lr * tc->embed_lr_scale, 0.f, 1};
-  a.seg[1] = {c->n_embed, c->n_matrix_end, lr * tc->matrix_lr_scale, tc->weight_decay, 1};
-  a.seg[2] = {c->n_matrix_end, c->n_params, lr, 0.f, 0};
+  if (shard) {  // chunk `rank` of every gradient segment: embedding, layers, gammas
+    const int nseg = static_cast<int>(c->segs.size());
+    if (nseg > rt::kMaxAdamSegments) return set_err(c, RT_ERR_SHAPE, "too many segments for the sharded AdamW");
+    for (int i = 0; i < nseg; ++i) {
+      const int64_t b = seg_own(c, i), e = b + seg_chunk(c, i);
+      if (i == 0)
+        a.seg[i] = {b, e, lr * tc->embed_lr_scale, 0.f, 1};
+      else if (i + 1 < nseg)
+        a.seg[i] = {b, e, lr * tc->matrix_lr_scale, tc->weight_decay, 1};
+      else
+        a.seg[i] = {b, e, lr, 0.f, 0};
+    }
+    a.nseg = nseg;
+  } else {
+    a.nseg = 3;
+    a.seg[0] = {0, c->n_embed, lr * tc->embed_lr_scale, 0.f, 1};
+    a.seg[1] = {c->n_embed, c->n_matrix_end, lr * tc->matrix_lr_scale, tc->weight_decay, 1};
+    a.seg[2] = {c->n_matrix_end, c->n_params, lr, 0.f, 0};
+  }
   a.beta1 = tc->beta1;
   a.beta2 = tc->beta2;
   a.eps = tc->eps;
@@ -1085,6 +1186,7 @@ RT_API int rt_weights_upload(rt_ctx* c, const rt_model_ptrs* w) {
     if ((rc = arena_h2d(c, c->params, w))) return rc;
     RT_LAUNCH(rt::cast_bf16(c->params, c->params_bf16, c->n_matrix_end, c->stream), "cast bf16");
     c->weights_set = true;
+    c->sharded_p = false;
   } else {
     // compact fp32 [embed | gammas]; this rank's matrix shard goes through a bounded fp32 staging buffer
     RT_CUDA(cudaMemcpyAsync(c->params, w->embed, sizeof(float) * c->n_embed, cudaMemcpyHostToDevice, c->stream), "upload embed");
@@ -1137,6 +1239,7 @@ RT_API int rt_weights_download(rt_ctx* c, const rt_model_ptrs* w) {
   int rc;
   if ((rc = check_train(c))) return rc;
   cudaSetDevice(c->device);
+  if ((rc = zero_gather(c, true, false, false))) return rc;
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   return arena_d2h(c, c->params, w);
 }
@@ -1146,6 +1249,7 @@ RT_API int rt_grads_download(rt_ctx* c, const rt_model_ptrs* g) {
   if ((rc = check_train(c))) return rc;
   cudaSetDevice(c->device);
   if ((rc = materialize_zero_grads(c))) return rc;
+  if ((rc = zero_gather(c, false, false, true))) return rc;
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   return arena_d2h(c, c->grads, g);
 }
@@ -1157,6 +1261,7 @@ RT_API int rt_grads_upload(rt_ctx* c, const rt_model_ptrs* g) {
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   if ((rc = arena_h2d(c, c->grads, g))) return rc;
   c->grads_zero_pending = false;
+  c->sharded_g = false;
   return RT_OK;
 }
 
@@ -1164,6 +1269,7 @@ RT_API int rt_opt_download(rt_ctx* c, const rt_model_ptrs* m, const rt_model_ptr
   int rc;
   if ((rc = check_train(c))) return rc;
   cudaSetDevice(c->device);
+  if ((rc = zero_gather(c, false, true, false))) return rc;
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   if ((rc = arena_d2h(c, c->mom1, m))) return rc;
   return arena_d2h(c, c->mom2, v);
@@ -1175,6 +1281,7 @@ RT_API int rt_opt_upload(rt_ctx* c, const rt_model_ptrs* m, const rt_model_ptrs*
   cudaSetDevice(c->device);
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   if ((rc = arena_h2d(c, c->mom1, m))) return rc;
+  c->sharded_mv = false;
   return arena_h2d(c, c->mom2, v);
 }
 
@@ -1190,6 +1297,7 @@ RT_API int rt_weights_init_normal(rt_ctx* c, uint64_t seed, float std) {
     RT_CUDA(cudaMemsetAsync(c->mom1, 0, sizeof(float) * c->n_params, c->stream), "zero m");
     RT_CUDA(cudaMemsetAsync(c->mom2, 0, sizeof(float) * c->n_params, c->stream), "zero v");
     c->grads_zero_pending = true;
+    c->sharded_p = c->sharded_mv = c->sharded_g = false;
   } else {
     // embed straight into the compact fp32 buffer; each matrix shard is generated at
     // the global indices of the full arena (same values as a training context / any TP degree)
@@ -1273,7 +1381,10 @@ RT_API int rt_backward(rt_ctx* c, float softcap, float loss_scale) {
   if ((rc = check_train(c))) return rc;
   if (!c->fwd_done) return set_err(c, RT_ERR_STATE, "backward before forward");
   cudaSetDevice(c->device);
+  // accumulating into gradients a sharded train step left: make them whole first
+  if (!c->grads_zero_pending && (rc = zero_gather(c, false, false, true))) return rc;
   if ((rc = backward_impl(c, softcap, loss_scale))) return rc;
+  if (c->grads_zero_pending) c->sharded_g = false;
   return wait_stream(c);
 }
 
@@ -1289,6 +1400,7 @@ RT_API int rt_grad_norm(rt_ctx* c, float* norm_out) {
   if ((rc = check_train(c))) return rc;
   cudaSetDevice(c->device);
   if ((rc = materialize_zero_grads(c))) return rc;
+  if ((rc = zero_gather(c, false, false, true))) return rc;
   RT_OTHER(2, rt::sumsq_norm(c->grads, c->n_params, c->norm_partials, c->d_norm, c->stream), "grad norm");
   RT_CUDA(cudaMemcpyAsync(c->h_loss + 1, c->d_norm, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "norm d2h");
   if ((rc = wait_stream(c))) return rc;
@@ -1313,6 +1425,7 @@ RT_API int rt_update_weights(rt_ctx* c, uint32_t t, float lr, const rt_train_con
   if (!tc || t == 0) return set_err(c, RT_ERR_ARG, "train config missing or t == 0");
   cudaSetDevice(c->device);
   if ((rc = materialize_zero_grads(c))) return rc;
+  if ((rc = zero_gather(c, true, true, true))) return rc;
   cudaEventRecord(c->ev[6], c->stream);
   if ((rc = adam_impl(c, t, lr, tc, grad_scale, nullptr, 0.f, 0.f))) return rc;
   cudaEventRecord(c->ev[7], c->stream);
@@ -1461,17 +1574,38 @@ static int train_step_device(rt_ctx* c, const rt::TokenBatch& tb, uint32_t step,
   if ((rc = forward_impl(c, batch, tc->softcap))) return rc;
   // data parallel: gradients are all-reduced bucket by bucket inside the backward
   c->overlap_allreduce = c->world > 1 && c->dist_mode == RT_DIST_DATA_PARALLEL;
+  const bool shard = c->overlap_allreduce && c->zero;
   c->layer_sumsq = true;  // grad-norm partials of each segment as soon as it is final
   rc = backward_impl(c, tc->softcap, tc->loss_scale);
   c->overlap_allreduce = false;
   c->layer_sumsq = false;
   if (rc) return rc;
   cudaEventRecord(c->ev[6], c->stream);
-  RT_OTHER(1, rt::sumsq_finish(c->norm_partials, (c->cfg.nlayers + 2) * rt::sumsq_seg_blocks(), c->d_norm, c->stream),
-           "grad norm");
+  const int nparts = (c->cfg.nlayers + 2) * rt::sumsq_seg_blocks();
+  if (shard) {  // this rank's sum of squares, summed over the ranks, then the square root
+    RT_OTHER(1, rt::sumsq_finish_sq(c->norm_partials, nparts, c->d_sumsq, c->stream), "grad norm");
+    if ((rc = nccl_ok(c, rt::nccl_api()->allReduce(c->d_sumsq, c->d_sumsq, 1, ncclFloat64, ncclSum, c->nccl->comm,
+                                                   c->stream),
+                      "ncclAllReduce")))
+      return rc;
+    RT_OTHER(1, rt::sqrt_to_float(c->d_sumsq, c->d_norm, c->stream), "grad norm");
+  } else {
+    RT_OTHER(1, rt::sumsq_finish(c->norm_partials, nparts, c->d_norm, c->stream), "grad norm");
+  }
   const float gsc = 1.0f / (static_cast<float>(batch) * static_cast<float>(c->world) * tc->loss_scale);
   const float lr = rt_learning_rate(step, tc);
-  if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip))) return rc;
+  if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip, shard))) return rc;
+  if (shard) {  // the weights the next forward reads, whole on every rank
+    const int nseg = static_cast<int>(c->segs.size());
+    rc = nccl_group(c, [&] {
+      int r = gather_seg(c, c->params, false, nseg - 1, c->stream);  // gammas (fp32)
+      if (r == RT_OK) r = gather_seg(c, c->params, false, 0, c->stream);  // embedding (fp32, the gather reads it)
+      for (int i = 0; r == RT_OK && i + 1 < nseg; ++i) r = gather_seg(c, c->params_bf16, true, i, c->stream);
+      return r;
+    });
+    if (rc) return rc;
+    c->sharded_p = c->sharded_mv = c->sharded_g = true;
+  }
   cudaEventRecord(c->ev[7], c->stream);
   c->ev_recorded |= 8u;
   if (!loss_out) return RT_OK;
@@ -1599,6 +1733,20 @@ RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id
   if (r != ncclSuccess) {
     c->nccl->comm = nullptr;
     return set_err(c, RT_ERR_NCCL, std::string("ncclCommInitRank: ") + api->errorString(r));
+  }
+  if (mode == RT_DIST_DATA_PARALLEL && !forward_only(c)) {
+    // shard the optimizer when every gradient segment splits into 16-byte-aligned
+    // chunks, one per rank (RUSTANE_DP_ALLREDUCE=1 keeps the all-reduce of every gradient)
+    c->segs.clear();
+    c->segs.push_back({0, c->n_embed});
+    for (const auto& o : c->layer_off) c->segs.push_back({o.wqkv, o.w2 + int64_t(c->cfg.dim) * c->cfg.hidden});
+    c->segs.push_back({c->n_matrix_end, c->n_params});
+    bool ok = api->reduceScatter && api->allGather && !getenv("RUSTANE_DP_ALLREDUCE") &&
+              static_cast<int>(c->segs.size()) <= rt::kMaxAdamSegments;
+    for (const auto& sg : c->segs) ok = ok && (sg.second - sg.first) % (int64_t(4) * world) == 0;
+    if (ok && !c->d_sumsq) c->d_sumsq = dalloc<double>(c, 1);
+    c->zero = ok && c->d_sumsq;
+    c->sharded_p = c->sharded_mv = c->sharded_g = false;
   }
   return RT_OK;
 }

@@ -145,6 +145,15 @@ struct rt_ctx {
   // distributed
   int world = 1, rank = 0, dist_mode = -1, timeout_ms = 0;
   rt::NcclState* nccl = nullptr;
+  // Data-parallel optimizer sharding: every gradient segment (embedding, each
+  // layer's matrices, the gammas) is reduce-scattered, rank r runs AdamW on chunk r
+  // of every segment, then the weights the forward reads (bf16 copy, fp32
+  // embedding and gammas) are all-gathered.  The fp32 matrices, the moments and
+  // the gradients stay sharded until a call that reads them whole gathers them.
+  bool zero = false;
+  bool sharded_p = false, sharded_mv = false, sharded_g = false;
+  std::vector<std::pair<int64_t, int64_t>> segs;  // arena ranges [embed, layer 0 .. L-1, gammas]
+  double* d_sumsq = nullptr;                      // [1] sum of squares of the gradients, all ranks
 
   // streams and events of the overlapped backward
   cudaStream_t s_dw = nullptr;    // weight-gradient GEMMs

@@ -1,6 +1,8 @@
 """Data-parallel train step on 2 GPUs through the C ABI (rt_dist_init + NCCL
-all-reduce inside rt_train_step): two ranks with one sequence each must match
-one GPU stepping on both sequences.  Skipped on boxes with fewer than 2 GPUs.
+inside rt_train_step: gradients reduce-scattered, AdamW sharded, weights
+all-gathered): two ranks with one sequence each must match one GPU stepping on
+both sequences -- losses, gradients, weights and the AdamW moments (downloaded
+whole, which gathers the shards).  Skipped on boxes with fewer than 2 GPUs.
 
 The two runs sum the same per-token terms in a different order (each rank's
 GEMMs see half the tokens, then the all-reduce adds the halves), so the
@@ -66,9 +68,11 @@ def _rank(rank, world, port, out):
         g = k.download_grads()  # all-reduced gradients of step 0
         losses.append(k.train_step(tok[rank * S:(rank + 1) * S], tgt[rank * S:(rank + 1) * S], 1, tc))
         w = k.download_weights()
+        opt = k.download_opt()  # the sharded AdamW moments, gathered
         if rank == 0:
             np.savez(out, losses=np.array(losses), **{n: a for n, a in w.tensors()},
-                     **{"grad_" + n: a for n, a in g.tensors()})
+                     **{"grad_" + n: a for n, a in g.tensors()}, **{"m_" + n: a for n, a in opt.m.tensors()},
+                     **{"v_" + n: a for n, a in opt.v.tensors()})
         else:
             np.save(out + ".rank1_losses.npy", np.array(losses))
         k.close()
@@ -92,6 +96,7 @@ def test_dp2_matches_single_gpu(tmp_path):
     g = k.download_grads()
     losses.append(k.train_step(tok, tgt, 1, tc))
     w = k.download_weights()
+    opt = k.download_opt()
     # rt_train_step returns this rank's loss; their mean is the loss over both sequences
     both = 0.5 * (got["losses"] + np.load(out + ".rank1_losses.npy"))
     np.testing.assert_allclose(both, losses, rtol=1e-5, atol=1e-6)
@@ -102,3 +107,7 @@ def test_dp2_matches_single_gpu(tmp_path):
     for (name, a), (_, a0) in zip(w.tensors(), w0.tensors()):
         u1, u2 = a - a0, got[name] - a0
         assert np.linalg.norm(u1 - u2) <= 0.05 * np.linalg.norm(u1) + 1e-7, name
+    for pre, t in (("m_", opt.m), ("v_", opt.v)):  # moments of the scaled gradients: same bound
+        for name, a in t.tensors():
+            b = got[pre + name]
+            assert np.linalg.norm(a - b) <= 0.05 * np.linalg.norm(a) + 1e-12, pre + name
