@@ -273,6 +273,7 @@ def main() -> None:
     with ClockSampler(local) as clocks:
         ev0.record(stream)
         staged_steps(K)
+        k._check(L.rt_join(k.handle))  # the last step's weight all-gathers (sharded data parallel) count too
         ev1.record(stream)
         loss_last = ctypes.c_float()
         k._check(L.rt_sync(k.handle, ctypes.byref(loss_last)))

@@ -186,6 +186,11 @@ RT_API int rt_stage_batch(rt_ctx* ctx, int slot, const uint32_t* tokens, const u
 RT_API int rt_train_step_staged(rt_ctx* ctx, int slot, uint32_t step, const rt_train_config* tc, float* loss_out);
 RT_API int rt_forward_staged(rt_ctx* ctx, int slot, float softcap);
 RT_API int rt_sync(rt_ctx* ctx, float* loss_out);
+/* Make the context stream wait for work the last step left on the context's
+ * other streams (the weight all-gathers of a sharded data-parallel step, which
+ * the next forward otherwise waits for layer by layer).  Asynchronous: an event
+ * recorded on the context stream after it covers the whole step. */
+RT_API int rt_join(rt_ctx* ctx);
 /* The context's CUDA stream (cudaStream_t) — every kernel of the context runs on it. */
 RT_API int rt_ctx_stream(const rt_ctx* ctx, void** stream_out);
 /* Bytes the last host-token call copied host -> device. */

@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
     "rt_nccl_unique_id": (c_int, [c_uint8_p]),
     "rt_dist_init": (c_int, [c_void_p, c_int, c_int, c_uint8_p, c_int, c_int]),
     "rt_grad_allreduce": (c_int, [c_void_p]),
+    "rt_join": (c_int, [c_void_p]),
     "rt_tokens_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_void_p)]),
     "rt_tokens_close": (c_int, [c_void_p]),
     "rt_tokens_len": (c_int, [c_void_p, ctypes.POINTER(c_int64)]),

@@ -216,9 +216,20 @@ float alpha_of(const rt_model_config& cfg) { return 1.0f / std::sqrt(2.0f * stat
 // contexts keep [embed | gammas] in a compact fp32 buffer.
 float* gamma_base(rt_ctx* c) { return c->params + (forward_only(c) ? c->n_embed : c->n_matrix_end); }
 
+// The main stream waits for the weight all-gathers a sharded train step left on
+// the comm stream (asynchronous; the next forward waits for them layer by layer
+// instead).
+void join_gathers(rt_ctx* c) {
+  if (c->gather_pending) {
+    cudaStreamWaitEvent(c->stream, c->ev_gather_all, 0);
+    c->gather_pending = false;
+  }
+}
+
 // Wait for the stream; with a communicator, poll so that a stuck collective
 // aborts after timeout_ms instead of blocking forever.
 int wait_stream(rt_ctx* c) {
+  join_gathers(c);
   if (!c->nccl || !c->nccl->comm) {
     cudaError_t e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return cuda_err(c, e, "stream synchronize");
@@ -561,10 +572,16 @@ int forward_impl(rt_ctx* c, int batch, float softcap) {
   const int D = cfg.dim, V = cfg.vocab, M = batch * cfg.seq;
   int rc;
   cudaEventRecord(c->ev[0], c->stream);
+  const bool pend = c->gather_pending;  // weights of the last sharded step still arriving, segment by segment
+  if (pend) {
+    cudaStreamWaitEvent(c->stream, c->ev_gather_seg.back(), 0);  // gammas
+    cudaStreamWaitEvent(c->stream, c->ev_gather_seg[0], 0);      // embedding (fp32 and bf16)
+  }
   float* x0 = c->acts[0].x;
   RT_OTHER(1, rt::embed_gather(c->params, c->cur->tokens, x0, M, D, V, c->d_err, c->stream), "embed gather");
   float* x = x0;
   for (int l = 0; l < cfg.nlayers; ++l) {
+    if (pend) cudaStreamWaitEvent(c->stream, c->ev_gather_seg[1 + l], 0);
     const rt::LayerActs& A = forward_only(c) ? c->acts[0] : c->acts[l];
     float* x_next;
     if (forward_only(c))
@@ -586,6 +603,7 @@ int forward_impl(rt_ctx* c, int batch, float softcap) {
   }
   RT_OTHER(1, rt::ce_forward(c->logits, c->cur->targets, c->row_loss, c->row_lse, M, V, softcap, c->stream), "ce fwd");
   RT_OTHER(1, rt::mean_reduce(c->row_loss, M, c->d_loss, c->stream), "loss mean");
+  if (pend) c->gather_pending = false;  // every segment has been waited for
   cudaEventRecord(c->ev[1], c->stream);
   c->ev_recorded |= 1u;
   c->cur_batch = batch;
@@ -652,6 +670,7 @@ int nccl_group(rt_ctx* c, F&& body) {
 // Collective: make the sharded arrays whole again on every rank (fp32 matrices
 // and embedding / gammas, moments, gradients) before a call that reads them.
 int zero_gather(rt_ctx* c, bool params, bool moments, bool grads) {
+  join_gathers(c);
   const int nseg = static_cast<int>(c->segs.size());
   const bool gp = params && c->sharded_p, gm = moments && c->sharded_mv, gg = grads && c->sharded_g;
   if (!gp && !gm && !gg) return RT_OK;
@@ -907,7 +926,7 @@ float powi_f32(float b, uint32_t t) {
 }
 
 int adam_impl(rt_ctx* c, uint32_t t, float lr, const rt_train_config* tc, float grad_scale, const float* d_norm,
-              float gsc, float clip, bool shard = false) {
+              float gsc, float clip, bool shard = false, int only_seg = -1) {
   rt::AdamArgs a;
   a.param = c->params;
   a.grad = c->grads;
@@ -917,16 +936,17 @@ int adam_impl(rt_ctx* c, uint32_t t, float lr, const rt_train_config* tc, float 
   if (shard) {  // chunk `rank` of every gradient segment: embedding, layers, gammas
     const int nseg = static_cast<int>(c->segs.size());
     if (nseg > rt::kMaxAdamSegments) return set_err(c, RT_ERR_SHAPE, "too many segments for the sharded AdamW");
+    a.nseg = 0;
     for (int i = 0; i < nseg; ++i) {
+      if (only_seg >= 0 && i != only_seg) continue;
       const int64_t b = seg_own(c, i), e = b + seg_chunk(c, i);
       if (i == 0)
-        a.seg[i] = {b, e, lr * tc->embed_lr_scale, 0.f, 1};
+        a.seg[a.nseg++] = {b, e, lr * tc->embed_lr_scale, 0.f, 1};
       else if (i + 1 < nseg)
-        a.seg[i] = {b, e, lr * tc->matrix_lr_scale, tc->weight_decay, 1};
+        a.seg[a.nseg++] = {b, e, lr * tc->matrix_lr_scale, tc->weight_decay, 1};
       else
-        a.seg[i] = {b, e, lr, 0.f, 0};
+        a.seg[a.nseg++] = {b, e, lr, 0.f, 0};
     }
-    a.nseg = nseg;
   } else {
     a.nseg = 3;
     a.seg[0] = {0, c->n_embed, lr * tc->embed_lr_scale, 0.f, 1};
@@ -1158,10 +1178,11 @@ RT_API int rt_ctx_destroy(rt_ctx* c) {
   for (auto& e : c->ev)
     if (e) cudaEventDestroy(e);
   for (auto e : c->event_pool) cudaEventDestroy(e);
-  for (auto* v : {&c->ev_dgate, &c->ev_rms2, &c->ev_attn, &c->ev_dw_done, &c->ev_comm})
+  for (auto* v : {&c->ev_dgate, &c->ev_rms2, &c->ev_attn, &c->ev_dw_done, &c->ev_comm, &c->ev_adam_seg,
+                  &c->ev_gather_seg})
     for (auto e : *v)
       if (e) cudaEventDestroy(e);
-  for (cudaEvent_t e : {c->ev_ce, c->ev_de, c->ev_main_done, c->ev_comm_all})
+  for (cudaEvent_t e : {c->ev_ce, c->ev_de, c->ev_main_done, c->ev_comm_all, c->ev_gather_all})
     if (e) cudaEventDestroy(e);
   if (c->s_dw) cudaStreamDestroy(c->s_dw);
   if (c->s_comm) cudaStreamDestroy(c->s_comm);
@@ -1179,6 +1200,7 @@ RT_API int rt_ctx_device_bytes(const rt_ctx* c, int64_t* out) {
 RT_API int rt_weights_upload(rt_ctx* c, const rt_model_ptrs* w) {
   if (!c || !w) return RT_ERR_ARG;
   cudaSetDevice(c->device);
+  join_gathers(c);
   const auto& cfg = c->cfg;
   const int64_t D = cfg.dim;
   int rc;
@@ -1258,6 +1280,7 @@ RT_API int rt_grads_upload(rt_ctx* c, const rt_model_ptrs* g) {
   int rc;
   if ((rc = check_train(c))) return rc;
   cudaSetDevice(c->device);
+  join_gathers(c);
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   if ((rc = arena_h2d(c, c->grads, g))) return rc;
   c->grads_zero_pending = false;
@@ -1279,6 +1302,7 @@ RT_API int rt_opt_upload(rt_ctx* c, const rt_model_ptrs* m, const rt_model_ptrs*
   int rc;
   if ((rc = check_train(c))) return rc;
   cudaSetDevice(c->device);
+  join_gathers(c);
   RT_CUDA(cudaStreamSynchronize(c->stream), "sync");
   if ((rc = arena_h2d(c, c->mom1, m))) return rc;
   c->sharded_mv = false;
@@ -1288,6 +1312,7 @@ RT_API int rt_opt_upload(rt_ctx* c, const rt_model_ptrs* m, const rt_model_ptrs*
 RT_API int rt_weights_init_normal(rt_ctx* c, uint64_t seed, float std) {
   if (!c) return RT_ERR_ARG;
   cudaSetDevice(c->device);
+  join_gathers(c);
   const int64_t D = c->cfg.dim;
   const int64_t n_gam = c->n_params - c->n_matrix_end;
   if (!forward_only(c)) {
@@ -1594,16 +1619,32 @@ static int train_step_device(rt_ctx* c, const rt::TokenBatch& tb, uint32_t step,
   }
   const float gsc = 1.0f / (static_cast<float>(batch) * static_cast<float>(c->world) * tc->loss_scale);
   const float lr = rt_learning_rate(step, tc);
-  if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip, shard))) return rc;
-  if (shard) {  // the weights the next forward reads, whole on every rank
+  if (!shard) {
+    if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip))) return rc;
+  } else {
+    // AdamW segment by segment in the order the next forward needs the weights
+    // (gammas, embedding, layers), each followed on the comm stream by the
+    // all-gather of what the forward reads: fp32 gammas, fp32 + bf16 embedding,
+    // bf16 layer matrices.  The next forward waits per segment.
     const int nseg = static_cast<int>(c->segs.size());
-    rc = nccl_group(c, [&] {
-      int r = gather_seg(c, c->params, false, nseg - 1, c->stream);  // gammas (fp32)
-      if (r == RT_OK) r = gather_seg(c, c->params, false, 0, c->stream);  // embedding (fp32, the gather reads it)
-      for (int i = 0; r == RT_OK && i + 1 < nseg; ++i) r = gather_seg(c, c->params_bf16, true, i, c->stream);
-      return r;
-    });
-    if (rc) return rc;
+    for (int k = 0; k < nseg; ++k) {
+      const int i = k == 0 ? nseg - 1 : k - 1;
+      if ((rc = adam_impl(c, step + 1, lr, tc, 1.0f, c->d_norm, gsc, tc->grad_clip, true, i))) return rc;
+      cudaEventRecord(c->ev_adam_seg[i], c->stream);
+    }
+    for (int k = 0; k < nseg; ++k) {
+      const int i = k == 0 ? nseg - 1 : k - 1;
+      cudaStreamWaitEvent(c->s_comm, c->ev_adam_seg[i], 0);
+      rc = nccl_group(c, [&] {
+        if (i == nseg - 1) return gather_seg(c, c->params, false, i, c->s_comm);
+        int r = i == 0 ? gather_seg(c, c->params, false, 0, c->s_comm) : RT_OK;
+        return r ? r : gather_seg(c, c->params_bf16, true, i, c->s_comm);
+      });
+      if (rc) return rc;
+      cudaEventRecord(c->ev_gather_seg[i], c->s_comm);
+    }
+    cudaEventRecord(c->ev_gather_all, c->s_comm);
+    c->gather_pending = true;
     c->sharded_p = c->sharded_mv = c->sharded_g = true;
   }
   cudaEventRecord(c->ev[7], c->stream);
@@ -1672,6 +1713,13 @@ RT_API int rt_sync(rt_ctx* c, float* loss_out) {
   if (loss_out) RT_CUDA(cudaMemcpyAsync(c->h_loss, c->d_loss, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "loss");
   if ((rc = wait_stream(c))) return rc;
   if (loss_out) *loss_out = c->h_loss[0];
+  return RT_OK;
+}
+
+RT_API int rt_join(rt_ctx* c) {
+  if (!c) return RT_ERR_ARG;
+  cudaSetDevice(c->device);
+  join_gathers(c);
   return RT_OK;
 }
 
@@ -1745,6 +1793,13 @@ RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id
               static_cast<int>(c->segs.size()) <= rt::kMaxAdamSegments;
     for (const auto& sg : c->segs) ok = ok && (sg.second - sg.first) % (int64_t(4) * world) == 0;
     if (ok && !c->d_sumsq) c->d_sumsq = dalloc<double>(c, 1);
+    if (ok && c->ev_adam_seg.empty()) {
+      c->ev_adam_seg.resize(c->segs.size());
+      c->ev_gather_seg.resize(c->segs.size());
+      for (auto* v : {&c->ev_adam_seg, &c->ev_gather_seg})
+        for (auto& e : *v) ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+      ok = ok && cudaEventCreateWithFlags(&c->ev_gather_all, cudaEventDisableTiming) == cudaSuccess;
+    }
     c->zero = ok && c->d_sumsq;
     c->sharded_p = c->sharded_mv = c->sharded_g = false;
   }

@@ -154,6 +154,13 @@ struct rt_ctx {
   bool sharded_p = false, sharded_mv = false, sharded_g = false;
   std::vector<std::pair<int64_t, int64_t>> segs;  // arena ranges [embed, layer 0 .. L-1, gammas]
   double* d_sumsq = nullptr;                      // [1] sum of squares of the gradients, all ranks
+  // Sharded step tail: AdamW of segment i on the main stream records ev_adam_seg[i];
+  // the comm stream gathers segment i after it and records ev_gather_seg[i]; the
+  // next forward waits segment by segment (gather_pending), every other reader
+  // waits for ev_gather_all.
+  std::vector<cudaEvent_t> ev_adam_seg, ev_gather_seg;
+  cudaEvent_t ev_gather_all = nullptr;
+  bool gather_pending = false;
 
   // streams and events of the overlapped backward
   cudaStream_t s_dw = nullptr;    // weight-gradient GEMMs
