@@ -90,27 +90,6 @@ struct DqSmem {
   static constexpr int BYTES = BAR + 128 + 1024;
 };
 
-// 2-D tiled bulk tensor store shared -> global (bulk-group completion).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* smem_src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(tm)),
-               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read_all() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// 32 values as bf16 into chunks 4c .. 4c+3 of row r of a 128-byte-swizzled tile (row base `row`).
-__device__ __forceinline__ void store_chunk32(uint8_t* row, int c, int r, const float (&v)[32]) {
-#pragma unroll
-  for (int u = 0; u < 4; ++u)
-    *reinterpret_cast<uint4*>(row + (((c * 4 + u) ^ (r & 7)) << 4)) =
-        make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
-                   pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
-}
-
 // ------------------------------------------------------------------ dK, dV
 __global__ void __launch_bounds__(kKvThreads, 1)
     attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,

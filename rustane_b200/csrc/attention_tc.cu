@@ -20,7 +20,8 @@
 //               written to shared memory in the 128-byte-swizzled K-major
 //               layout the MMA reads, running sum l; O rescaled in TMEM only
 //               when the row max grew by more than 2^8 (otherwise the stale
-//               max is kept: P <= 256).
+//               max is kept: P <= 256); O / l goes through a swizzled shared-
+//               memory tile to one TMA store per 64 columns.
 // All waits are bounded; a timeout sets the device error word.
 #include "attention.h"
 #include "common.cuh"
@@ -66,8 +67,8 @@ __device__ __forceinline__ void softmax_bar() {  // the 8 softmax warps only
 }
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
-    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, int D, __nv_bfloat16* __restrict__ out,
-                       int64_t ldo, float* __restrict__ lse2, int S, int nh, float scale_log2, int* err) {
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_out,
+                       float* __restrict__ lse2, int S, int nh, float scale_log2, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + FwdSmem::BAR);
@@ -98,7 +99,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_qkv);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_out);
+  }
   if (warp == 2) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -111,6 +115,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // --------------------------------------------------------------- producer
+      const int D = nh * kHd;
       const int qc = h * kHd, kc = D + h * kHd, vc = 2 * D + h * kHd;
       int issued = 0;  // key blocks whose K and V loads were issued
       mbar_arrive_expect_tx(&bar[kQFull], kTileBytes);
@@ -297,23 +302,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (!ok) {
       if (lane == 0) set_error(err, kDevTimeoutEpilogue);
     } else {
+      // O / l in bf16 into the (now idle) P tile, 128-byte swizzled, head-dim columns
+      // [64 hh, 64 hh + 64) = atom hh; one TMA store per atom below
       tc_fence_after();
       const float inv_l = 1.f / l;
-      __nv_bfloat16* orow = out + static_cast<int64_t>(tok0 + q0 + r) * ldo + h * kHd + hh * 64;
-#pragma unroll 1
+      uint8_t* orow = smem + FwdSmem::P + hh * kAtomBytes + r * 128;
+#pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
+        float f[32];
         tmem_ld32(tmem + 2 * kBlk + lane_off + hh * 64 + c * 32, o);
         tmem_ld_wait();
-        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          dst[u] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * u]) * inv_l, __uint_as_float(o[8 * u + 1]) * inv_l),
-                              pack_bf16x2(__uint_as_float(o[8 * u + 2]) * inv_l, __uint_as_float(o[8 * u + 3]) * inv_l),
-                              pack_bf16x2(__uint_as_float(o[8 * u + 4]) * inv_l, __uint_as_float(o[8 * u + 5]) * inv_l),
-                              pack_bf16x2(__uint_as_float(o[8 * u + 6]) * inv_l, __uint_as_float(o[8 * u + 7]) * inv_l));
+        for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(o[e]) * inv_l;
+        store_chunk32(orow, c, r, f);
       }
+      fence_proxy_async_smem();
       if (hh == 0) lse2[(static_cast<int64_t>(b) * nh + h) * S + q0 + r] = m_used + log2f(l);
+    }
+    softmax_bar();  // every softmax warp has written its rows (failed warps skip only their work)
+    if (threadIdx.x == 128 && !*abort_flag) {
+      tma_store_2d(&tm_out, smem + FwdSmem::P, h * kHd, tok0 + q0);
+      tma_store_2d(&tm_out, smem + FwdSmem::P + kAtomBytes, h * kHd + 64, tok0 + q0);
+      bulk_commit();
+      bulk_wait_read_all();
     }
     tc_fence_before();
   }
@@ -328,18 +340,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }  // namespace
 
 int attn_forward(const AttnArgs& a, cudaStream_t s) {
-  if (a.S % kBlk != 0 || a.hd != kHd || a.D != a.heads * kHd || a.ldq % 8 != 0) return -1;
-  CUtensorMap tm;
-  if (!make_tmap_bf16(&tm, a.qkv, static_cast<uint64_t>(3) * a.D, static_cast<uint64_t>(a.batch) * a.S, a.ldq, 64,
-                      kBlk))
+  if (a.S % kBlk != 0 || a.hd != kHd || a.D != a.heads * kHd || a.ldq % 8 != 0 || a.ldo % 8 != 0) return -1;
+  if (reinterpret_cast<uintptr_t>(a.out) & 15) return -1;
+  CUtensorMap tm, tm_out;
+  const uint64_t M = static_cast<uint64_t>(a.batch) * a.S;
+  if (!make_tmap_bf16(&tm, a.qkv, static_cast<uint64_t>(3) * a.D, M, a.ldq, 64, kBlk) ||
+      !make_tmap_bf16(&tm_out, a.out, static_cast<uint64_t>(a.D), M, a.ldo, 64, kBlk))
     return -3;
   static const cudaError_t attr =
       cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdSmem::BYTES);
   if (attr != cudaSuccess) return attr;
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kHd));
   dim3 grid(a.heads, a.batch, a.S / kBlk);
-  attn_fwd_tc_kernel<<<grid, kFwdThreads, FwdSmem::BYTES, s>>>(tm, a.D, a.out, a.ldo, a.lse2, a.S, a.heads, scale_log2,
-                                                            a.err);
+  attn_fwd_tc_kernel<<<grid, kFwdThreads, FwdSmem::BYTES, s>>>(tm, tm_out, a.lse2, a.S, a.heads, scale_log2, a.err);
   return cudaGetLastError();
 }
 
