@@ -300,56 +300,56 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       }
       return w;
     };
+    // Per sub-block: both TMEM tiles (S^T and dP^T) are loaded under one wait, P^T and
+    // dS^T are computed together and published with one proxy fence -- the chain of
+    // dependent latencies per sub-block, not the arithmetic, bounds this loop.
     for (int t = 0; ok && t < n; ++t) {
-      const int st = t & 1, qs = t % kQStages;
+      const int st = t & 1;
       const uint32_t ph = (t >> 1) & 1;
       const int q0 = (t0 + t) * kSub + hh * 32;  // first query of this thread's 32 columns
       // lse2 and rowsum of this warp's 32 queries: lane e holds query q0 + e (read from L2, shared by shuffles)
       const float l_lane = __ldg(lse2 + stat0 + q0 + lane), d_lane = __ldg(rowsum + stat0 + q0 + lane);
-      if (!wait(&bar[kQFull + qs], (t / kQStages) & 1) || !wait(&bar[kSFull + st], ph)) break;
+      if (!wait(&bar[kSFull + st], ph) || !wait(&bar[kDpFull + st], ph)) break;
       tc_fence_after();
-      uint32_t v[32];
+      uint32_t v[32], w[32];
       tmem_ld32(tmem + kColS + st * kSub + lane_off + hh * 32, v);
+      tmem_ld32(tmem + kColDp + st * kSub + lane_off + hh * 32, w);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kSFree + st]);
-      float p[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float pe = exp2f(__uint_as_float(v[e]) * scale_log2 - __shfl_sync(0xffffffffu, l_lane, e));
-        p[e] = q0 + e >= kpos ? pe : 0.f;  // causal: query before key -> 0
+      if (lane == 0) {
+        mbar_arrive(&bar[kSFree + st]);
+        mbar_arrive(&bar[kDpFree + st]);
       }
-      // P^T row r, columns 32 hh .. +31: 4 chunks of 16 B, chunk c at (c ^ r % 8) * 16
-      if (!wait(&bar[kPFree], (t & 1) ^ 1)) break;
+      uint32_t pk[16], dk[16];  // P^T and dS^T of this thread's 32 columns, bf16 pairs
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float pr[2], dr[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float pe = exp2f(__uint_as_float(v[e + x]) * scale_log2 - __shfl_sync(0xffffffffu, l_lane, e + x));
+          pr[x] = q0 + e + x >= kpos ? pe : 0.f;  // causal: query before key -> 0
+          dr[x] = pr[x] * (__uint_as_float(w[e + x]) - __shfl_sync(0xffffffffu, d_lane, e + x));
+        }
+        pk[e / 2] = pack_bf16x2(pr[0], pr[1]);
+        dk[e / 2] = pack_bf16x2(dr[0], dr[1]);
+      }
+      // rows r of P^T and dS^T, columns 32 hh .. +31: 4 chunks of 16 B, chunk c at (c ^ r % 8) * 16
+      if (!wait(&bar[kPFree], (t & 1) ^ 1) || !wait(&bar[kDsFree], (t & 1) ^ 1)) break;
       uint8_t* prow = smem + KvSmem::P + r * 128;
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        *reinterpret_cast<uint4*>(prow + (((hh * 4 + u) ^ (r & 7)) << 4)) =
-            make_uint4(pack_bf16x2(p[8 * u], p[8 * u + 1]), pack_bf16x2(p[8 * u + 2], p[8 * u + 3]),
-                       pack_bf16x2(p[8 * u + 4], p[8 * u + 5]), pack_bf16x2(p[8 * u + 6], p[8 * u + 7]));
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kPFull]);
-      if (!wait(&bar[kDpFull + st], ph)) break;
-      tc_fence_after();
-      tmem_ld32(tmem + kColDp + st * kSub + lane_off + hh * 32, v);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kDpFree + st]);
-#pragma unroll
-      for (int e = 0; e < 32; ++e) p[e] = p[e] * (__uint_as_float(v[e]) - __shfl_sync(0xffffffffu, d_lane, e));
-      if (!wait(&bar[kDsFree], (t & 1) ^ 1)) break;
       uint8_t* drow = smem + KvSmem::DS + r * 128;
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        *reinterpret_cast<uint4*>(drow + (((hh * 4 + u) ^ (r & 7)) << 4)) =
-            make_uint4(pack_bf16x2(p[8 * u], p[8 * u + 1]), pack_bf16x2(p[8 * u + 2], p[8 * u + 3]),
-                       pack_bf16x2(p[8 * u + 4], p[8 * u + 5]), pack_bf16x2(p[8 * u + 6], p[8 * u + 7]));
+      for (int u = 0; u < 4; ++u) {
+        const int off = ((hh * 4 + u) ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        *reinterpret_cast<uint4*>(drow + off) = make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+      }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kDsFull]);
+      if (lane == 0) {
+        mbar_arrive(&bar[kPFull]);
+        mbar_arrive(&bar[kDsFull]);
+      }
     }
     // RoPE tables of this key position for head-dim pairs [32 hh, 32 hh + 32), loaded
     // while the last MMAs run
