@@ -1479,7 +1479,8 @@ int check_layer(rt_ctx* c, int layer) {
   if (layer < 0 || layer >= c->cfg.nlayers) return set_err(c, RT_ERR_ARG, "layer index out of range");
   if (!c->weights_set) return set_err(c, RT_ERR_STATE, "weights not uploaded");
   if (c->tp) return set_err(c, RT_ERR_STATE, "single-layer calls run on unsharded contexts");
-  return RT_OK;
+  cudaSetDevice(c->device);
+  return zero_gather(c, true, true, true);  // a sharded data-parallel step left them in chunks (collective)
 }
 
 // Forward of layer `l` on host input x (reference layout); output left in c->x_out.
@@ -1812,6 +1813,8 @@ RT_API int rt_grad_allreduce(rt_ctx* c) {
   if (c->world == 1) return RT_OK;
   if (!c->nccl || !c->nccl->comm) return set_err(c, RT_ERR_NCCL, "no communicator (aborted or not initialised)");
   if ((rc = materialize_zero_grads(c))) return rc;
+  // after a sharded train step each rank holds the summed gradients of its chunks: gathering them is the sum
+  if (c->sharded_g) return zero_gather(c, false, false, true);
   rt::NcclApi* api = rt::nccl_api();
   ncclResult_t r = api->allReduce(c->grads, c->grads, static_cast<size_t>(c->n_params), ncclFloat32, ncclSum,
                                   c->nccl->comm, c->stream);
