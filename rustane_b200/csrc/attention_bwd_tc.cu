@@ -7,25 +7,24 @@
 // then the RoPE backward rotation of dK and dQ.  Two kernels:
 //
 // attn_bwd_kv_tc_kernel — one CTA per (head, sequence, block of 128 keys),
-// looping over the 64-query sub-blocks at or after the keys (causal):
-//   warp 0      TMA producer: K and V once, then Q_t, dO_t (64 x 128) into a
-//               four-deep ring;
-//   warp 1      one lane issues the MMAs: S^T_t = K Q_t^T and dP^T_t = V dO_t^T
-//               into double-buffered TMEM tiles (128 keys x 64 queries), then
-//               dV += P^T_t dO_t and dK += dS^T_t Q_t into TMEM accumulators;
-//               S^T / dP^T of sub-block t+1 are issued before dV / dK of t, so
-//               the tensor pipe works while the elementwise warps handle t;
-//   warp 2      owns the TMEM allocation (512 columns);
-//   warp 3      stores each dS^T tile (bf16) to the scratch with TMA, for the dQ kernel;
-//   warps 4-11  elementwise: two threads per key row (TMEM lane = key), 32
-//               queries each: P^T = exp2(S^T * scale_log2 - lse2) (causal mask),
-//               dS^T = P^T * (dP^T - rowsum), both written in bf16 into shared
-//               memory in the 128-byte-swizzled K-major layout the MMA reads
-//               (one tile each: the MMA that reads tile t finishes long before
-//               tile t+1 is ready); lse2 / rowsum come from L2, one per lane,
-//               passed around by shuffles;
-//               at the end dV and dK (scale, RoPE backward) go from TMEM through
-//               swizzled shared-memory tiles to dqkv by TMA stores.
+// looping over the 128-query blocks at or after the keys (causal):
+//   warp 0      TMA producer: K and V once, then Q_t, dO_t (128 x 128) into a
+//               two-deep ring;
+//   warp 1      one lane issues the MMAs, all 128 x 128 x 16 (the full tensor
+//               rate): S^T_t = K Q_t^T and dP^T_t = V dO_t^T into TMEM, then
+//               dV += P^T_t dO_t with P^T read from TMEM (the elementwise warps
+//               write it in bf16 over their own S^T columns) and dK += dS^T_t Q_t;
+//               issue order dV(t), S^T(t+1), dK(t), dP^T(t+1);
+//   warp 2      owns the TMEM allocation (512 columns: S^T / P^T, dP^T, dV, dK);
+//   warp 3      stores each dS^T tile (bf16, two 64-query halves) to the scratch
+//               with TMA, for the dQ kernel;
+//   warps 4-11  elementwise: two threads per key row (TMEM lane = key), 64
+//               queries each: P^T = exp2(S^T * scale_log2 - lse2) (causal mask)
+//               back into TMEM, dS^T = P^T * (dP^T - rowsum) in bf16 into shared
+//               memory in the 128-byte-swizzled K-major layout the MMA reads;
+//               lse2 / rowsum come from L2, two per lane, passed around by
+//               shuffles; at the end dV and dK (scale, RoPE backward) go from
+//               TMEM through swizzled shared-memory tiles to dqkv by TMA stores.
 //
 // attn_bwd_dq_tc_kernel — one CTA per (head, sequence, block of 128 queries):
 //   dQ = sum over key blocks j of dS_j K_j (both operands MN-major in shared
@@ -47,10 +46,6 @@ constexpr int kKeys = 128;                     // keys per kv CTA (and per dQ st
 constexpr int kSub = 64;                       // queries per sub-block
 constexpr int kKvTile = kKeys * kHd * 2;       // 32 KB: two 64-column atoms of 128 rows
 constexpr int kKvAtom = kKvTile / 2;           // 16 KB
-constexpr int kQTile = kSub * kHd * 2;         // 16 KB: two 64-column atoms of 64 rows
-constexpr int kQAtom = kQTile / 2;             // 8 KB
-constexpr int kPTile = kKeys * kSub * 2;       // 16 KB: 128 key rows x 64 queries, one atom
-constexpr int kQStages = 4;                    // Q / dO ring depth
 constexpr int kKvThreads = 384;
 constexpr int kDqThreads = 256;
 constexpr int kDqStages = 3;
@@ -58,30 +53,28 @@ constexpr int kDqStages = 3;
 struct KvSmem {
   static constexpr int K = 0;
   static constexpr int V = K + kKvTile;
-  static constexpr int Q = V + kKvTile;               // [kQStages]
-  static constexpr int DO = Q + kQStages * kQTile;     // [kQStages]
-  static constexpr int P = DO + kQStages * kQTile;     // one P^T tile
-  static constexpr int DS = P + kPTile;                // one dS^T tile
-  static constexpr int BAR = DS + kPTile;
+  static constexpr int Q = V + kKvTile;        // [2] 128-query tiles
+  static constexpr int DO = Q + 2 * kKvTile;   // [2]
+  static constexpr int DS = DO + 2 * kKvTile;  // dS^T: 128 keys x 128 queries, two 64-query atoms
+  static constexpr int BAR = DS + kKvTile;
   static constexpr int BYTES = BAR + 256 + 1024;
 };
 static_assert(KvSmem::BYTES <= 232448, "kv kernel shared memory");
 
 enum KvBar : int {
   kKvFull = 0,
-  kQFull = 1,     // [kQStages] Q and dO of a sub-block
-  kQEmpty = 5,    // [kQStages]
-  kSFull = 9,     // [2] S^T in TMEM
-  kSFree = 11,    // [2]
-  kDpFull = 13,   // [2] dP^T in TMEM
-  kDpFree = 15,   // [2]
-  kPFull = 17,    // P^T in shared memory
-  kPFree = 18,
-  kDsFull = 19,   // dS^T in shared memory
-  kDsFree = 20,   // dK MMA done and the tile stored
-  kAccFull = 21,
-  kKvDrain = 22,
-  kKvNumBars = 23
+  kQFull = 1,    // [2] Q and dO of a 128-query block
+  kQEmpty = 3,   // [2]
+  kSFull = 5,    // S^T in TMEM
+  kSFree = 6,    // dV of the block done: its P^T (over the S^T columns) consumed
+  kDpFull = 7,   // dP^T in TMEM
+  kDpFree = 8,
+  kPFull = 9,    // P^T in TMEM
+  kDsFull = 10,  // dS^T in shared memory
+  kDsFree = 11,  // dK MMA done and the tile stored
+  kAccFull = 12,
+  kKvDrain = 13,
+  kKvNumBars = 14
 };
 
 struct DqSmem {
@@ -91,12 +84,33 @@ struct DqSmem {
 };
 
 // ------------------------------------------------------------------ dK, dV
+// TMEM operand A of tcgen05.mma: D (+)= A[tmem] * B[smem desc] (A: 128 lanes = M rows,
+// K elements as bf16 pairs, 8 columns per K = 16).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Each thread of the warp writes 16 consecutive 32-bit columns of its own TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __global__ void __launch_bounds__(kKvThreads, 1)
-    attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
-                          const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_ds,
-                          const __grid_constant__ CUtensorMap tm_out, const float* __restrict__ lse2,
-                          const float* __restrict__ rowsum, int D, int S, int nh, float scale, float scale_log2,
-                          const float* __restrict__ cosb, const float* __restrict__ sinb, int* err) {
+    attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_do,
+                          const __grid_constant__ CUtensorMap tm_ds, const __grid_constant__ CUtensorMap tm_out,
+                          const float* __restrict__ lse2, const float* __restrict__ rowsum, int D, int S, int nh,
+                          float scale, float scale_log2, const float* __restrict__ cosb,
+                          const float* __restrict__ sinb, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + KvSmem::BAR);
@@ -106,8 +120,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y, j = blockIdx.z;  // key block 0 has the most work: dispatched first
   const int nsub = S / kSub, nkb = S / kKeys;
-  const int t0 = 2 * j;           // first sub-block at or after the keys
-  const int n = nsub - t0;        // sub-blocks this CTA visits
+  const int n = nkb - j;  // 128-query blocks at or after the keys
   const int tok0 = b * S;
   const int k0 = j * kKeys;
   const int bh = b * nh + h;
@@ -115,18 +128,15 @@ __global__ void __launch_bounds__(kKvThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[kKvFull], 1);
-    for (int i = 0; i < kQStages; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar[kQFull + i], 1);
       mbar_init(&bar[kQEmpty + i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar[kSFull + i], 1);
-      mbar_init(&bar[kSFree + i], 8);
-      mbar_init(&bar[kDpFull + i], 1);
-      mbar_init(&bar[kDpFree + i], 8);
-    }
+    mbar_init(&bar[kSFull], 1);
+    mbar_init(&bar[kSFree], 1);
+    mbar_init(&bar[kDpFull], 1);
+    mbar_init(&bar[kDpFree], 8);
     mbar_init(&bar[kPFull], 8);
-    mbar_init(&bar[kPFree], 1);
     mbar_init(&bar[kDsFull], 8);
     mbar_init(&bar[kDsFree], 2);
     mbar_init(&bar[kAccFull], 1);
@@ -136,7 +146,6 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_kv);
-    tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_ds);
     tma_prefetch_desc(&tm_out);
@@ -148,7 +157,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // TMEM columns: S^T [0,64) [64,128), dP^T [128,192) [192,256), dV [256,384), dK [384,512)
+  // TMEM columns: S^T (then P^T in bf16 pairs) [0,128), dP^T [128,256), dV [256,384), dK [384,512)
   const uint32_t tmem = *tmem_slot;
   constexpr uint32_t kColS = 0, kColDp = 128, kColDv = 256, kColDk = 384;
 
@@ -163,97 +172,112 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       tma_load_2d(smem + KvSmem::V, &tm_kv, &bar[kKvFull], vc, tok0 + k0);
       tma_load_2d(smem + KvSmem::V + kKvAtom, &tm_kv, &bar[kKvFull], vc + 64, tok0 + k0);
       for (int t = 0; t < n; ++t) {
-        const int st = t % kQStages;
-        const uint32_t ph = (t / kQStages) & 1;
+        const int st = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
         if (!mbar_wait(&bar[kQEmpty + st], ph ^ 1) || *abort_flag) {
           set_error(err, kDevTimeoutProducer);
           *abort_flag = 1;
           break;
         }
-        const int q0 = (t0 + t) * kSub;
+        const int q0 = (j + t) * kKeys;
         uint64_t* fb = &bar[kQFull + st];
-        mbar_arrive_expect_tx(fb, 2 * kQTile);
-        uint8_t* sq = smem + KvSmem::Q + st * kQTile;
-        uint8_t* sd = smem + KvSmem::DO + st * kQTile;
-        tma_load_2d(sq, &tm_q, fb, qc, tok0 + q0);
-        tma_load_2d(sq + kQAtom, &tm_q, fb, qc + 64, tok0 + q0);
+        mbar_arrive_expect_tx(fb, 2 * kKvTile);
+        uint8_t* sq = smem + KvSmem::Q + st * kKvTile;
+        uint8_t* sd = smem + KvSmem::DO + st * kKvTile;
+        tma_load_2d(sq, &tm_kv, fb, qc, tok0 + q0);
+        tma_load_2d(sq + kKvAtom, &tm_kv, fb, qc + 64, tok0 + q0);
         tma_load_2d(sd, &tm_do, fb, h * kHd, tok0 + q0);
-        tma_load_2d(sd + kQAtom, &tm_do, fb, h * kHd + 64, tok0 + q0);
+        tma_load_2d(sd + kKvAtom, &tm_do, fb, h * kHd + 64, tok0 + q0);
         issued = t + 1;
       }
       if (*abort_flag) {  // let copies still in flight land before the CTA exits
         mbar_wait(&bar[kKvFull], 0);
-        for (int t = (issued > kQStages ? issued - kQStages : 0); t < issued; ++t)
-          mbar_wait(&bar[kQFull + t % kQStages], (t / kQStages) & 1);
+        for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t) mbar_wait(&bar[kQFull + (t & 1)], (t >> 1) & 1);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc_s = idesc_bf16_f32(kKeys, kSub, false, false);  // K / V rows, Q / dO rows
-      constexpr uint32_t idesc_a = idesc_bf16_f32(kKeys, kHd, false, true);   // P^T / dS^T, dO / Q hd-contiguous
+      // per 128-query block t: S^T = K Q^T, dP^T = V dO^T (all 128 x 128 x 128, full rate);
+      // dV += P^T dO with P^T read from TMEM; dK += dS^T Q.  Issue order dV(t), S^T(t+1),
+      // dK(t), dP^T(t+1): the next block's S^T is ready while the elementwise warps finish dS^T(t).
+      constexpr uint32_t idesc_kk = idesc_bf16_f32(kKeys, kKeys, false, false);
+      constexpr uint32_t idesc_kn = idesc_bf16_f32(kKeys, kHd, false, true);
       const uint32_t sk = smem_u32(smem + KvSmem::K), sv = smem_u32(smem + KvSmem::V);
-      bool ok = mbar_wait(&bar[kKvFull], 0);
-      auto issue_s = [&](int t) -> bool {  // S^T_t and dP^T_t
-        const int st = t & 1, qs = t % kQStages;
-        const uint32_t ph = (t >> 1) & 1;
-        if (!mbar_wait(&bar[kQFull + qs], (t / kQStages) & 1) || !mbar_wait(&bar[kSFree + st], ph ^ 1) || *abort_flag)
-          return false;
-        tc_fence_after();
-        const uint32_t sq = smem_u32(smem + KvSmem::Q + qs * kQTile);
-        const uint32_t sd = smem_u32(smem + KvSmem::DO + qs * kQTile);
+      const uint32_t sds = smem_u32(smem + KvSmem::DS);
+      auto qaddr = [&](int t) { return smem_u32(smem + KvSmem::Q + (t & 1) * kKvTile); };
+      auto daddr = [&](int t) { return smem_u32(smem + KvSmem::DO + (t & 1) * kKvTile); };
+      auto issue_st = [&](int t) {
+        const uint32_t sq = qaddr(t);
 #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk) {
-          const uint32_t ka = (kk >> 2) * kKvAtom + (kk & 3) * 32, kb = (kk >> 2) * kQAtom + (kk & 3) * 32;
-          umma_bf16(tmem + kColS + st * kSub, smem_desc_sw128(sk + ka, 16, 1024), smem_desc_sw128(sq + kb, 16, 1024),
-                    idesc_s, kk != 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * kKvAtom + (kk & 3) * 32;
+          umma_bf16(tmem + kColS, smem_desc_sw128(sk + off, 16, 1024), smem_desc_sw128(sq + off, 16, 1024), idesc_kk,
+                    kk != 0 ? 1u : 0u);
         }
-        umma_commit(&bar[kSFull + st]);
-        if (!mbar_wait(&bar[kDpFree + st], ph ^ 1) || *abort_flag) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kHd / 16; ++kk) {
-          const uint32_t ka = (kk >> 2) * kKvAtom + (kk & 3) * 32, kb = (kk >> 2) * kQAtom + (kk & 3) * 32;
-          umma_bf16(tmem + kColDp + st * kSub, smem_desc_sw128(sv + ka, 16, 1024), smem_desc_sw128(sd + kb, 16, 1024),
-                    idesc_s, kk != 0 ? 1u : 0u);
-        }
-        umma_commit(&bar[kDpFull + st]);
-        return true;
+        umma_commit(&bar[kSFull]);
       };
-      ok = ok && issue_s(0);
+      auto issue_dp = [&](int t) {
+        const uint32_t sd = daddr(t);
+#pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kKvAtom + (kk & 3) * 32;
+          umma_bf16(tmem + kColDp, smem_desc_sw128(sv + off, 16, 1024), smem_desc_sw128(sd + off, 16, 1024), idesc_kk,
+                    kk != 0 ? 1u : 0u);
+        }
+        umma_commit(&bar[kDpFull]);
+      };
+      bool ok = mbar_wait(&bar[kKvFull], 0) && mbar_wait(&bar[kQFull], 0) && !*abort_flag;
+      if (ok) {
+        tc_fence_after();
+        issue_st(0);
+        issue_dp(0);
+      }
       for (int t = 0; ok && t < n; ++t) {
-        if (t + 1 < n && !issue_s(t + 1)) {
-          ok = false;
-          break;
-        }
-        const int qs = t % kQStages;
-        const uint32_t sq = smem_u32(smem + KvSmem::Q + qs * kQTile);
-        const uint32_t sd = smem_u32(smem + KvSmem::DO + qs * kQTile);
-        // dV += P^T dO: P^T K-major over the 64 queries, dO hd-contiguous (two 64-wide blocks 8 KB apart)
-        if (!mbar_wait(&bar[kPFull], t & 1) || *abort_flag) {
+        const int ph = t & 1;
+        // dV += P^T dO: P^T of query k-chunk kk sits in TMEM columns 8 kk (queries < 64) or 64 + 8 (kk - 4)
+        if (!mbar_wait(&bar[kPFull], ph) || *abort_flag) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sp = smem_u32(smem + KvSmem::P);
+        const uint32_t sd = daddr(t), sq = qaddr(t);
 #pragma unroll
-        for (int kk = 0; kk < kSub / 16; ++kk)
-          umma_bf16(tmem + kColDv, smem_desc_sw128(sp + kk * 32, 16, 1024), smem_desc_sw128(sd + kk * 2048, kQAtom, 1024),
-                    idesc_a, (t | kk) != 0 ? 1u : 0u);
-        umma_commit(&bar[kPFree]);
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint32_t acol = kColS + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
+          umma_bf16_ts(tmem + kColDv, tmem + acol, smem_desc_sw128(sd + kk * 2048, kKvAtom, 1024), idesc_kn,
+                       (t | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&bar[kSFree]);
+        if (t + 1 < n) {  // S^T(t+1) overwrites P^T(t): after dV(t)
+          if (!mbar_wait(&bar[kQFull + ((t + 1) & 1)], ((t + 1) >> 1) & 1) || !mbar_wait(&bar[kSFree], ph) ||
+              *abort_flag) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_st(t + 1);
+        }
         // dK += dS^T Q
-        if (!mbar_wait(&bar[kDsFull], t & 1) || *abort_flag) {
+        if (!mbar_wait(&bar[kDsFull], ph) || *abort_flag) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sds = smem_u32(smem + KvSmem::DS);
 #pragma unroll
-        for (int kk = 0; kk < kSub / 16; ++kk)
-          umma_bf16(tmem + kColDk, smem_desc_sw128(sds + kk * 32, 16, 1024),
-                    smem_desc_sw128(sq + kk * 2048, kQAtom, 1024), idesc_a, (t | kk) != 0 ? 1u : 0u);
+        for (int kk = 0; kk < kKeys / 16; ++kk)
+          umma_bf16(tmem + kColDk, smem_desc_sw128(sds + (kk >> 2) * kKvAtom + (kk & 3) * 32, 16, 1024),
+                    smem_desc_sw128(sq + kk * 2048, kKvAtom, 1024), idesc_kn, (t | kk) != 0 ? 1u : 0u);
         umma_commit(&bar[kDsFree]);
-        umma_commit(&bar[kQEmpty + qs]);
+        umma_commit(&bar[kQEmpty + (t & 1)]);
+        if (t + 1 < n) {  // dP^T(t+1) overwrites dP^T(t): after the elementwise warps have read it
+          if (!mbar_wait(&bar[kDpFree], ph) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_dp(t + 1);
+        }
       }
       if (!ok) {
         set_error(err, kDevTimeoutMma);
@@ -267,12 +291,14 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   } else if (warp == 3) {
     if (lane == 0) {
       // ------------------------------------------------- dS^T tiles -> scratch
-      // scratch row of (sequence-head bh, key block j, sub-block i): ((bh * nkb + j) * nsub + i) * 128
+      // scratch row of (sequence-head bh, key block j, 64-query sub-block i): ((bh * nkb + j) * nsub + i) * 128;
+      // the two 64-query halves of block t are sub-blocks 2 (j + t) and 2 (j + t) + 1
       int t = 0;
       for (; t < n; ++t) {
         if (!mbar_wait(&bar[kDsFull], t & 1) || *abort_flag) break;
-        const int row = ((bh * nkb + j) * nsub + t0 + t) * kKeys;
+        const int row = ((bh * nkb + j) * nsub + 2 * (j + t)) * kKeys;
         tma_store_2d(&tm_ds, smem + KvSmem::DS, 0, row);
+        tma_store_2d(&tm_ds, smem + KvSmem::DS + kKvAtom, 0, row + kKeys);
         bulk_commit();
         bulk_wait_read_all();
         mbar_arrive(&bar[kDsFree]);
@@ -286,7 +312,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   } else if (warp >= 4) {
     // -------------------------------------------------------------- elementwise
     const int qw = warp & 3;            // TMEM lane quadrant: key rows 32 qw ..
-    const int hh = (warp - 4) >> 2;     // query columns [32 hh, 32 hh + 32) of a sub-block
+    const int hh = (warp - 4) >> 2;     // query columns [64 hh, 64 hh + 64) of a block
     const int r = qw * 32 + lane;       // key row within the block
     const int kpos = k0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
@@ -300,56 +326,64 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       }
       return w;
     };
-    // Per sub-block: both TMEM tiles (S^T and dP^T) are loaded under one wait, P^T and
-    // dS^T are computed together and published with one proxy fence -- the chain of
-    // dependent latencies per sub-block, not the arithmetic, bounds this loop.
     for (int t = 0; ok && t < n; ++t) {
-      const int st = t & 1;
-      const uint32_t ph = (t >> 1) & 1;
-      const int q0 = (t0 + t) * kSub + hh * 32;  // first query of this thread's 32 columns
-      // lse2 and rowsum of this warp's 32 queries: lane e holds query q0 + e (read from L2, shared by shuffles)
-      const float l_lane = __ldg(lse2 + stat0 + q0 + lane), d_lane = __ldg(rowsum + stat0 + q0 + lane);
-      if (!wait(&bar[kSFull + st], ph) || !wait(&bar[kDpFull + st], ph)) break;
+      const uint32_t ph = t & 1;
+      const int q0 = (j + t) * kKeys + hh * 64;  // first query of this thread's 64 columns
+      // lse2 and rowsum of this warp's 64 queries: lane e holds queries q0 + e and q0 + 32 + e (from L2)
+      const float l0 = __ldg(lse2 + stat0 + q0 + lane), l1 = __ldg(lse2 + stat0 + q0 + 32 + lane);
+      const float d0 = __ldg(rowsum + stat0 + q0 + lane), d1 = __ldg(rowsum + stat0 + q0 + 32 + lane);
+      if (!wait(&bar[kSFull], ph)) break;
       tc_fence_after();
-      uint32_t v[32], w[32];
-      tmem_ld32(tmem + kColS + st * kSub + lane_off + hh * 32, v);
-      tmem_ld32(tmem + kColDp + st * kSub + lane_off + hh * 32, w);
-      tmem_ld_wait();
+      float p[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + kColS + lane_off + hh * 64 + c * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float pe = exp2f(__uint_as_float(v[e]) * scale_log2 - __shfl_sync(0xffffffffu, c ? l1 : l0, e));
+          p[c * 32 + e] = q0 + c * 32 + e >= kpos ? pe : 0.f;  // causal: query before key -> 0
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(p[c * 32 + 2 * e], p[c * 32 + 2 * e + 1]);
+        // P^T in bf16 pairs over this thread's own S^T columns (chunk 0, already read)
+        tmem_st16(tmem + kColS + lane_off + hh * 64 + c * 16, pk);
+      }
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar[kSFree + st]);
-        mbar_arrive(&bar[kDpFree + st]);
-      }
-      uint32_t pk[16], dk[16];  // P^T and dS^T of this thread's 32 columns, bf16 pairs
+      if (lane == 0) mbar_arrive(&bar[kPFull]);
+      if (!wait(&bar[kDpFull], ph)) break;
+      tc_fence_after();
+      uint32_t dk[32];  // dS^T of the 64 columns, bf16 pairs
 #pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        float pr[2], dr[2];
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + kColDp + lane_off + hh * 64 + c * 32, v);
+        tmem_ld_wait();
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float pe = exp2f(__uint_as_float(v[e + x]) * scale_log2 - __shfl_sync(0xffffffffu, l_lane, e + x));
-          pr[x] = q0 + e + x >= kpos ? pe : 0.f;  // causal: query before key -> 0
-          dr[x] = pr[x] * (__uint_as_float(w[e + x]) - __shfl_sync(0xffffffffu, d_lane, e + x));
+        for (int e = 0; e < 32; e += 2) {
+          const float x0 = p[c * 32 + e] * (__uint_as_float(v[e]) - __shfl_sync(0xffffffffu, c ? d1 : d0, e));
+          const float x1 =
+              p[c * 32 + e + 1] * (__uint_as_float(v[e + 1]) - __shfl_sync(0xffffffffu, c ? d1 : d0, e + 1));
+          dk[c * 16 + e / 2] = pack_bf16x2(x0, x1);
         }
-        pk[e / 2] = pack_bf16x2(pr[0], pr[1]);
-        dk[e / 2] = pack_bf16x2(dr[0], dr[1]);
       }
-      // rows r of P^T and dS^T, columns 32 hh .. +31: 4 chunks of 16 B, chunk c at (c ^ r % 8) * 16
-      if (!wait(&bar[kPFree], (t & 1) ^ 1) || !wait(&bar[kDsFree], (t & 1) ^ 1)) break;
-      uint8_t* prow = smem + KvSmem::P + r * 128;
-      uint8_t* drow = smem + KvSmem::DS + r * 128;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kDpFree]);
+      // dS^T row r, query atom hh (64 columns = 128 B): chunk u at (u ^ r % 8) * 16
+      if (!wait(&bar[kDsFree], ph ^ 1)) break;
+      uint8_t* drow = smem + KvSmem::DS + hh * kKvAtom + r * 128;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int off = ((hh * 4 + u) ^ (r & 7)) << 4;
-        *reinterpret_cast<uint4*>(prow + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        *reinterpret_cast<uint4*>(drow + off) = make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
-      }
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(drow + ((u ^ (r & 7)) << 4)) =
+            make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar[kPFull]);
-        mbar_arrive(&bar[kDsFull]);
-      }
+      if (lane == 0) mbar_arrive(&bar[kDsFull]);
     }
     // RoPE tables of this key position for head-dim pairs [32 hh, 32 hh + 32), loaded
     // while the last MMAs run
@@ -363,7 +397,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     if (!ok && lane == 0) set_error(err, kDevTimeoutEpilogue);
     if (ok) {
       tc_fence_after();
-      // dK (scale, RoPE backward) and dV rows -> bf16 tiles in the (now idle) Q / dO ring, 128-byte
+      // dK (scale, RoPE backward) and dV rows -> bf16 tiles in the (now idle) Q ring, 128-byte
       // swizzled, head-dim columns [64 hh, 64 hh + 64) = atom hh; then TMA stores into dqkv
       uint8_t* tk = smem + KvSmem::Q + hh * kKvAtom + r * 128;
       uint8_t* tv = smem + KvSmem::Q + kKvTile + hh * kKvAtom + r * 128;
@@ -380,10 +414,10 @@ __global__ void __launch_bounds__(kKvThreads, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float d0 = __uint_as_float(v[e]) * scale, d1 = __uint_as_float(v[e + 1]) * scale;
+          const float e0 = __uint_as_float(v[e]) * scale, e1 = __uint_as_float(v[e + 1]) * scale;
           const float cc = rc[c * 16 + e / 2], ss = rs[c * 16 + e / 2];
-          f[e] = cc * d0 + ss * d1;
-          f[e + 1] = -ss * d0 + cc * d1;
+          f[e] = cc * e0 + ss * e1;
+          f[e + 1] = -ss * e0 + cc * e1;
         }
         store_chunk32(tk, c, r, f);
       }
@@ -580,10 +614,9 @@ int attn_backward_tc(const AttnArgs& a, cudaStream_t s) {
     return -1;
   const uint64_t M = static_cast<uint64_t>(a.batch) * a.S;
   const uint64_t ds_rows = static_cast<uint64_t>(a.batch) * a.heads * a.S * a.S / kSub;
-  CUtensorMap tm_kv, tm_q, tm_do, tm_ds, tm_ds2, tm_out;
+  CUtensorMap tm_kv, tm_do, tm_ds, tm_ds2, tm_out;
   if (!make_tmap_bf16(&tm_kv, a.qkv, 3 * static_cast<uint64_t>(a.D), M, a.ldq, 64, kKeys) ||
-      !make_tmap_bf16(&tm_q, a.qkv, 3 * static_cast<uint64_t>(a.D), M, a.ldq, 64, kSub) ||
-      !make_tmap_bf16(&tm_do, a.dout, static_cast<uint64_t>(a.D), M, a.lddo, 64, kSub) ||
+      !make_tmap_bf16(&tm_do, a.dout, static_cast<uint64_t>(a.D), M, a.lddo, 64, kKeys) ||
       !make_tmap_bf16(&tm_ds, a.ds_scratch, kSub, ds_rows, kSub, 64, kKeys) ||
       !make_tmap_bf16(&tm_ds2, a.ds_scratch, kSub, ds_rows, kSub, 64, 2 * kKeys) ||
       !make_tmap_bf16(&tm_out, a.dqkv, 3 * static_cast<uint64_t>(a.D), M, a.lddq, 64, kKeys))
@@ -599,8 +632,8 @@ int attn_backward_tc(const AttnArgs& a, cudaStream_t s) {
   const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(a.heads, a.batch, a.S / kKeys);
-  attn_bwd_kv_tc_kernel<<<grid, kKvThreads, KvSmem::BYTES, s>>>(tm_kv, tm_q, tm_do, tm_ds, tm_out, a.lse2, a.dvec,
-                                                               a.D, a.S, a.heads, scale, scale_log2, a.rope_cos_b,
+  attn_bwd_kv_tc_kernel<<<grid, kKvThreads, KvSmem::BYTES, s>>>(tm_kv, tm_do, tm_ds, tm_out, a.lse2, a.dvec, a.D,
+                                                               a.S, a.heads, scale, scale_log2, a.rope_cos_b,
                                                                a.rope_sin_b, a.err);
   attn_bwd_dq_tc_kernel<<<grid, kDqThreads, DqSmem::BYTES, s>>>(tm_kv, tm_ds2, tm_out, a.D, a.S, a.heads, scale,
                                                                a.rope_cos_b, a.rope_sin_b, a.err);
