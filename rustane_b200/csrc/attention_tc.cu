@@ -17,8 +17,9 @@
 //   warps 4-11  softmax, two threads per query row (TMEM lane = row, each
 //               thread 64 of the 128 key columns; row max and sum exchanged
 //               through shared memory): P_j = exp2(S_j * scale - m) in bf16
-//               written to shared memory in the 128-byte-swizzled K-major
-//               layout the MMA reads, running sum l; O rescaled in TMEM only
+//               pairs written back over the thread's own S_j columns in TMEM,
+//               where the P V MMA reads it as its TMEM operand (the MMA's
+//               commit frees the S buffer), running sum l; O rescaled in TMEM only
 //               when the row max grew by more than 2^8 (otherwise the stale
 //               max is kept: P <= 256); O / l goes through a swizzled shared-
 //               memory tile to one TMA store per 64 columns.
@@ -91,7 +92,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&bar[kVFull + i], 1);
       mbar_init(&bar[kVEmpty + i], 1);
       mbar_init(&bar[kSFull + i], 1);
-      mbar_init(&bar[kSFree + i], 8);
+      mbar_init(&bar[kSFree + i], 1);
     }
     mbar_init(&bar[kPFull], 8);
     mbar_init(&bar[kPvDone], 1);
@@ -159,7 +160,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idesc_s = idesc_bf16_f32(kBlk, kBlk, false, false);  // Q, K: both hd-contiguous
       constexpr uint32_t idesc_o = idesc_bf16_f32(kBlk, kHd, false, true);    // P key-contiguous, V hd-contiguous
       const uint32_t sq = smem_u32(smem + FwdSmem::Q);
-      const uint32_t sp = smem_u32(smem + FwdSmem::P);
       bool ok = mbar_wait(&bar[kQFull], 0);
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
@@ -192,13 +192,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t sv = smem_u32(smem + FwdSmem::V + st * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk) {
-          // P: K-major over keys (two 64-key atoms); V: hd-contiguous rows, 16 keys = 2 KB
-          const uint32_t poff = (kk >> 2) * kAtomBytes + (kk & 3) * 32;
-          umma_bf16(tmem + 2 * kBlk, smem_desc_sw128(sp + poff, 16, 1024),
-                    smem_desc_sw128(sv + kk * 2048, kAtomBytes, 1024), idesc_o, (j | kk) != 0 ? 1u : 0u);
+          // P from TMEM (bf16 pairs over the S_j columns: keys 16 kk.. at column 8 kk, or 64 + 8 (kk - 4)
+          // for the second half); V: hd-contiguous rows, 16 keys = 2 KB
+          const uint32_t acol = st * kBlk + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
+          umma_bf16_ts(tmem + 2 * kBlk, tmem + acol, smem_desc_sw128(sv + kk * 2048, kAtomBytes, 1024), idesc_o,
+                       (j | kk) != 0 ? 1u : 0u);
         }
         umma_commit(&bar[kVEmpty + st]);
         umma_commit(&bar[kPvDone]);
+        umma_commit(&bar[kSFree + st]);  // P_j (over S_j) consumed: the buffer can take S_{j+2}
       }
       if (!ok) {
         set_error(err, kDevTimeoutMma);
@@ -215,7 +217,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
     float* red = reinterpret_cast<float*>(smem + FwdSmem::RED);
     float* sum = reinterpret_cast<float*>(smem + FwdSmem::SUM);
-    uint8_t* prow = smem + FwdSmem::P + hh * kAtomBytes + r * 128;  // this thread's 64 P values
     float m_used = -INFINITY, l = 0.f;
     // A failed (timed-out) wait does not leave the loop: every softmax warp must
     // reach the same sequence of named barriers.  After the first failure the
@@ -274,24 +275,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         tmem_st_wait();
       }
-      // P = exp2(S * scale - m) in bf16: 8 chunks of 16 B, chunk u of row r at (u ^ r % 8) * 16
+      // P = exp2(S * scale - m) in bf16 pairs, written back over this thread's own (already
+      // read) S_j columns: keys 64 hh + 2 i, + 1 at column 64 hh + i; the P V MMA reads it there
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        uint32_t pk[4];
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int e = u * 8 + 2 * t;
+        for (int t = 0; t < 16; ++t) {
+          const int e = c * 32 + 2 * t;
           const float p0 = e <= lim ? exp2f(__uint_as_float(v[e]) * scale_log2 - m_used) : 0.f;
           const float p1 = e + 1 <= lim ? exp2f(__uint_as_float(v[e + 1]) * scale_log2 - m_used) : 0.f;
           l += p0 + p1;
           pk[t] = pack_bf16x2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st16(ts + c * 16, pk);
       }
+      tmem_st_wait();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kSFree + st]);
-      fence_proxy_async_smem();  // P writes -> visible to the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kPFull]);
     }
