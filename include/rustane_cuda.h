@@ -266,7 +266,10 @@ RT_API int rt_nccl_unique_id(uint8_t* out128);
  * rt_grads_download, rt_grad_norm, rt_clip_grads, rt_update_weights and an
  * accumulating rt_backward gather them first, so every rank must make those
  * calls together.  When a segment does not split into 16-byte chunks per rank
- * (or RUSTANE_DP_ALLREDUCE=1 is set), the gradients are all-reduced instead. */
+ * (or RUSTANE_DP_ALLREDUCE=1 is set), the gradients are all-reduced instead.
+ * A context joins one communicator: after a join with world > 1, a further
+ * call returns RT_ERR_STATE.  A failed join (RT_ERR_NCCL) leaves the context
+ * unchanged. */
 RT_API int rt_dist_init(rt_ctx* ctx, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms);
 /* Sum the gradients over the data-parallel ranks (one in-place all-reduce). */
 RT_API int rt_grad_allreduce(rt_ctx* ctx);

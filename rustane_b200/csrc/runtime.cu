@@ -1750,12 +1750,30 @@ RT_API int rt_nccl_unique_id(uint8_t* out128) {
 RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms) {
   if (!c || world <= 0 || rank < 0 || rank >= world) return RT_ERR_ARG;
   if (mode != RT_DIST_DATA_PARALLEL && mode != RT_DIST_TENSOR_PARALLEL) return RT_ERR_ARG;
+  if (c->nccl) return set_err(c, RT_ERR_STATE, "rt_dist_init was already called on this context");
+  const int nh = c->cfg.heads, units = c->cfg.hidden / 64;
   if (mode == RT_DIST_TENSOR_PARALLEL) {
-    // shard heads (uneven split allowed) and hidden columns (64-column units) over the ranks
     if (!forward_only(c)) return set_err(c, RT_ERR_STATE, "tensor parallelism needs a forward-only context");
     if (c->weights_set) return set_err(c, RT_ERR_STATE, "call rt_dist_init before uploading or initialising weights");
-    const int nh = c->cfg.heads, units = c->cfg.hidden / 64;
     if (world > nh || world > units) return set_err(c, RT_ERR_SHAPE, "more tensor-parallel ranks than heads");
+  }
+  // join the communicator before changing the context, so that a failed join leaves it as it was
+  rt::NcclApi* api = nullptr;
+  if (world > 1) {
+    if (!unique_id128) return RT_ERR_ARG;
+    api = rt::nccl_api();
+    if (!api) return set_err(c, RT_ERR_NCCL, "libnccl.so.2 could not be loaded");
+    cudaSetDevice(c->device);
+    ncclUniqueId id;
+    memcpy(&id, unique_id128, 128);
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = api->commInitRank(&comm, world, id, rank);
+    if (r != ncclSuccess) return set_err(c, RT_ERR_NCCL, std::string("ncclCommInitRank: ") + api->errorString(r));
+    c->nccl = new rt::NcclState();
+    c->nccl->comm = comm;
+  }
+  if (mode == RT_DIST_TENSOR_PARALLEL) {
+    // shard heads (uneven split allowed) and hidden columns (64-column units) over the ranks
     const int hb = nh / world, hr = nh % world, ub = units / world, ur = units % world;
     free_shard_buffers(c);
     c->tp = world > 1;
@@ -1771,18 +1789,6 @@ RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id
   c->dist_mode = mode;
   c->timeout_ms = timeout_ms;
   if (world == 1) return RT_OK;
-  if (!unique_id128) return RT_ERR_ARG;
-  rt::NcclApi* api = rt::nccl_api();
-  if (!api) return set_err(c, RT_ERR_NCCL, "libnccl.so.2 could not be loaded");
-  cudaSetDevice(c->device);
-  ncclUniqueId id;
-  memcpy(&id, unique_id128, 128);
-  c->nccl = new rt::NcclState();
-  ncclResult_t r = api->commInitRank(&c->nccl->comm, world, id, rank);
-  if (r != ncclSuccess) {
-    c->nccl->comm = nullptr;
-    return set_err(c, RT_ERR_NCCL, std::string("ncclCommInitRank: ") + api->errorString(r));
-  }
   if (mode == RT_DIST_DATA_PARALLEL && !forward_only(c)) {
     // shard the optimizer when every gradient segment splits into 16-byte-aligned
     // chunks, one per rank (RUSTANE_DP_ALLREDUCE=1 keeps the all-reduce of every gradient)

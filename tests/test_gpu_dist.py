@@ -61,6 +61,12 @@ def _rank(rank, world, port, out):
         uid = [CompiledKernels.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         k.dist_init(world, rank, uid[0], timeout_ms=60000)
+        from rustane_b200 import RustaneError, _lib
+        try:  # one communicator per context: a second join is refused before any NCCL call
+            k.dist_init(world, rank, uid[0], timeout_ms=60000)
+            raise AssertionError("a second rt_dist_init was accepted")
+        except RustaneError as e:
+            assert e.code == _lib.RT_ERR_STATE, e
         tok, tgt = _data()
         S = cfg.seq
         tc = TrainConfig(warmup_steps=2, total_steps=10)
