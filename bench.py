@@ -34,7 +34,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "train-step tok/s & forward ms at 600M/5B/7B; TC util vs B200 bf16 peak"
-# Published reference throughput (Apple M4 Max, ANE + CPU; BASELINE.md), tok/s at batch 1:
+# Published reference throughput (Apple M4 Max, ANE + CPU), tok/s at batch 1:
 PUBLISHED = {
     "600m": (533.0, "600m-A train step 533 tok/s (results/2026-03-18_1830_param-sweep.md:37)"),
     "5b": (74.0, "5b-B train step 74 tok/s (results/2026-03-18_1830_param-sweep.md:78)"),

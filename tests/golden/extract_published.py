@@ -48,7 +48,9 @@ def parse(root: Path) -> list[dict]:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/extract_published.py <reference-root>")
+    root = Path(sys.argv[1])
     rows = parse(root)
     OUT.write_text(json.dumps(rows, indent=1) + "\n")
     print(f"wrote {len(rows)} rows to {OUT}")
