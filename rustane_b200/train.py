@@ -19,9 +19,23 @@ target_1_5b besides gpt_karpathy / gpt_1024 / mha_28l / custom:dim,hidden,nlayer
 Each optimizer step runs the accum microbatches as one device batch
 (gradients summed over them, loss averaged): the same arithmetic as the
 reference's microbatch loop (bin/train.rs:283-301), one launch sequence.
+
+Data parallel (an addition; the reference trains on one device): launched by
+torchrun with WORLD_SIZE > 1, rank r takes the contiguous block of accum/world
+microbatches starting at r * accum/world on GPU LOCAL_RANK (--device is then
+ignored), the library sums the gradients over the ranks inside the step
+(rt_dist_init, data-parallel mode), and the printed loss is the mean of the
+ranks' losses -- the same step as one GPU running all accum microbatches.
+accum must be a multiple of the world size.  Every rank runs validation and
+takes part in the checkpoint and grad-norm gathers; rank 0 alone prints and
+writes files.
+
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m rustane_b200.train \\
+        --data train.bin --accum 8 ...
 """
 from __future__ import annotations
 
+import os
 import sys
 import time
 from dataclasses import dataclass, field
@@ -168,6 +182,58 @@ def train_config(a: Args) -> TrainConfig:
     return tc
 
 
+@dataclass
+class DistInfo:
+    """This process's place in a torchrun launch (one process per GPU)."""
+    world: int = 1
+    rank: int = 0
+    local_rank: int = 0
+
+    @classmethod
+    def from_env(cls, env=os.environ) -> "DistInfo":
+        world = int(env.get("WORLD_SIZE", "1"))
+        if world <= 1:
+            return cls()
+        return cls(world, int(env["RANK"]), int(env.get("LOCAL_RANK", env["RANK"])))
+
+
+def rank_micros(accum: int, world: int, rank: int) -> range:
+    """The microbatch indices of the reference's accum loop (bin/train.rs:284)
+    that `rank` runs: a contiguous block of accum / world."""
+    if accum % world:
+        raise UsageError(f"--accum {accum} is not a multiple of the {world} data-parallel ranks")
+    per = accum // world
+    return range(rank * per, (rank + 1) * per)
+
+
+class _Group:
+    """Host-side plumbing of a data-parallel CLI run over torch.distributed
+    (gloo: only the communicator id and one loss per step cross it; the
+    gradients move inside the library over NCCL)."""
+
+    def __init__(self, d: DistInfo):
+        import torch.distributed as tdist
+        self.d, self.tdist = d, tdist
+        self.owned = not tdist.is_initialized()
+        if self.owned:
+            tdist.init_process_group("gloo", rank=d.rank, world_size=d.world)
+
+    def join(self, kernels: CompiledKernels) -> None:
+        uid = [CompiledKernels.nccl_unique_id() if self.d.rank == 0 else None]
+        self.tdist.broadcast_object_list(uid, src=0)
+        kernels.dist_init(self.d.world, self.d.rank, uid[0], timeout_ms=120000)
+
+    def mean(self, x: float) -> float:
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.tdist.all_reduce(t)
+        return float(np.float32(t.item() / self.d.world))
+
+    def close(self) -> None:
+        if self.owned:
+            self.tdist.destroy_process_group()
+
+
 def f32sum(x: np.ndarray) -> np.float32:
     """Left-to-right f32 sum (Rust's Iterator::sum over f32)."""
     return np.cumsum(np.asarray(x, np.float32), dtype=np.float32)[-1] if len(x) else np.float32(0)
@@ -214,8 +280,23 @@ class RunResult:
     seconds: float = 0.0
 
 
-def run(a: Args, out=print) -> RunResult:
-    """main (bin/train.rs:298-446)."""
+def run(a: Args, out=print, dist: DistInfo | None = None) -> RunResult:
+    """main (bin/train.rs:298-446); data parallel over the ranks of `dist`
+    (default: the torchrun environment)."""
+    dist = dist if dist is not None else DistInfo.from_env()
+    tc = train_config(a)
+    micros = rank_micros(tc.accum_steps, dist.world, dist.rank)
+    if dist.rank != 0:
+        out = lambda s: None  # noqa: E731
+    group = _Group(dist) if dist.world > 1 else None
+    try:
+        return _run(a, tc, micros, dist, group, out)
+    finally:
+        if group is not None:
+            group.close()
+
+
+def _run(a: Args, tc: TrainConfig, micros: range, dist: DistInfo, group, out) -> RunResult:
     cfg = model_config(a.model)
     out("=== Rustane Trainer ===")
     out(f"model: {a.model} ({cfg.nlayers}L, {cfg.dim}D, {cfg.vocab}V, {cfg.seq}S)")
@@ -234,11 +315,14 @@ def run(a: Args, out=print) -> RunResult:
         out("Loading token_bytes...")
         token_bytes = TokenBytes.load(a.token_bytes_path)
 
-    tc = train_config(a)
     out("\nCreating the B200 context...")
     t0 = time.perf_counter()
-    max_batch = max(tc.accum_steps, min(max(a.val_steps, 1), 32))
-    kernels = CompiledKernels.compile(cfg, max_batch=max_batch, device=a.device)
+    max_batch = max(len(micros), min(max(a.val_steps, 1), 32))
+    device = dist.local_rank if group is not None else a.device
+    kernels = CompiledKernels.compile(cfg, max_batch=max_batch, device=device)
+    if group is not None:
+        group.join(kernels)
+        out(f"  data parallel: {dist.world} ranks x {len(micros)} microbatches")
     out(f"  ready in {time.perf_counter() - t0:.1f}s ({kernels.device_bytes() / 2**30:.1f} GiB on the device)")
 
     first_step = 0
@@ -275,10 +359,12 @@ def run(a: Args, out=print) -> RunResult:
     train_start = time.perf_counter()
     for step in range(first_step, tc.total_steps):
         step_t0 = time.perf_counter()
-        wins = [train_data.train_window(step, micro, seq) for micro in range(accum)]
+        wins = [train_data.train_window(step, micro, seq) for micro in micros]
         tok = np.concatenate([w[0] for w in wins])
         tgt = np.concatenate([w[1] for w in wins])
         avg_loss = kernels.train_step(tok, tgt, step, tc)
+        if group is not None:
+            avg_loss = group.mean(avg_loss)
         gnorm = float(np.float32(kernels.grad_norm()) * gsc)
         lr = learning_rate(step, tc)
         step_time = time.perf_counter() - step_t0
@@ -301,9 +387,10 @@ def run(a: Args, out=print) -> RunResult:
         if a.checkpoint_dir is not None and ((step + 1) % a.checkpoint_interval == 0 or last):
             weights = kernels.download_weights()
             opt = kernels.download_opt() if a.checkpoint_opt else None
-            path = save_checkpoint(cfg, weights, opt, step + 1, a.checkpoint_dir, with_opt=a.checkpoint_opt)
-            out(f"  saved checkpoint: {path} ({path.stat().st_size / 1e6:.1f} MB)")
-            res.checkpoints.append(path)
+            if dist.rank == 0:
+                path = save_checkpoint(cfg, weights, opt, step + 1, a.checkpoint_dir, with_opt=a.checkpoint_opt)
+                out(f"  saved checkpoint: {path} ({path.stat().st_size / 1e6:.1f} MB)")
+                res.checkpoints.append(path)
 
     res.seconds = time.perf_counter() - train_start
     out("\n=== Training complete ===")
@@ -322,6 +409,8 @@ def main(argv: list[str] | None = None) -> int:
     try:
         a = parse_args(sys.argv[1:] if argv is None else argv)
         model_config(a.model)
+        d = DistInfo.from_env()
+        rank_micros(train_config(a).accum_steps, d.world, d.rank)
     except UsageError as e:
         print(e, file=sys.stderr)
         return 1

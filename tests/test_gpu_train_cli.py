@@ -108,3 +108,46 @@ def test_sweep_writes_bench_result(tmp_path):
     assert res.fingerprint == br.compute_fingerprint(res)
     p = br.write_result(res, tmp_path / "bench-result.json", out=lambda s: None)
     assert p.read_text() == br.to_json(res, pretty=True)
+
+
+def _dp_rank(rank, port, root, ck):
+    import os
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from pathlib import Path
+    res = train.run(args(Path(root), "--steps", "3", "--val-interval", "100", "--ckpt-interval", "3", "--ckpt-dir",
+                         ck, "--ckpt-opt"), out=lambda s: None, dist=train.DistInfo(2, rank, rank))
+    if rank == 0:
+        np.save(Path(root) / "dp_losses.npy", np.array([res.losses, res.gnorms]))
+
+
+@pytest.mark.skipif(__import__("torch").cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_cli_data_parallel_matches_one_gpu(files):
+    """torchrun-style data parallelism in the CLI: two ranks with one of the
+    two microbatches each must give the losses, gradient norms and checkpoint
+    of one GPU running both (the summation order differs, so to rounding)."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_dp_rank, args=(port, str(files), str(files / "ck_dp")), nprocs=2, join=True)
+    losses, gnorms = np.load(files / "dp_losses.npy")
+    one = train.run(args(files, "--steps", "3", "--val-interval", "100", "--ckpt-interval", "3", "--ckpt-dir",
+                         str(files / "ck_one"), "--ckpt-opt"), out=lambda s: None)
+    # step 0 starts from the same weights; later steps from weights that AdamW moved
+    # a little differently (the gradients agree only to rounding)
+    assert abs(losses[0] - one.losses[0]) < 2e-5 and abs(gnorms[0] - one.gnorms[0]) < 1e-3 * one.gnorms[0]
+    np.testing.assert_allclose(losses, one.losses, rtol=0, atol=1e-3)
+    np.testing.assert_allclose(gnorms, one.gnorms, rtol=2e-2)
+    cfg = train.model_config(MODEL)
+    w_dp, opt_dp, step_dp, _ = load_checkpoint(files / "ck_dp" / "ckpt_000003.bin", cfg)
+    w_one, opt_one, step_one, _ = load_checkpoint(files / "ck_one" / "ckpt_000003.bin", cfg)
+    assert step_dp == step_one == 3
+    w0 = engine.random_weights(cfg)
+    for (name, a), (_, b), (_, a0) in zip(w_one.tensors(), w_dp.tensors(), w0.tensors()):
+        u1, u2 = a - a0, b - a0  # AdamW moves near-zero gradients by ~lr either way: compare whole updates
+        assert np.linalg.norm(u1 - u2) <= 0.05 * np.linalg.norm(u1) + 1e-7, name
+    for name, a in opt_one.m.tensors():
+        b = dict(opt_dp.m.tensors())[name]
+        assert np.linalg.norm(a - b) <= 0.05 * np.linalg.norm(a) + 1e-12, name

@@ -1,6 +1,8 @@
 """The training CLI's host logic (bin/train.rs:40-98, 298-366): flags,
 defaults, model selection, parameter count and the Rust number formats of
-its log lines.  No GPU."""
+its log lines, and the host side of a data-parallel run (the microbatch
+split over ranks, the loss mean over gloo ranks).  No GPU."""
+import numpy as np
 import pytest
 
 from rustane_b200 import train
@@ -67,3 +69,49 @@ def test_rust_number_formats():
     assert [json_f32(x) for x in (961.0, 0.1, 533.3333, 1e-7, 1.5e30, 0.001234, 0.0)] == \
         ["961.0", "0.1", "533.3333", "1e-7", "1.5e30", "0.001234", "0.0"]
     assert json_f64(579.716608) == "579.716608" and json_f64(float("nan")) == "null"
+
+
+def test_rank_micros_partition_the_accum_loop():
+    for accum, world in ((8, 8), (8, 2), (6, 3), (4, 1)):
+        blocks = [train.rank_micros(accum, world, r) for r in range(world)]
+        assert [m for b in blocks for m in b] == list(range(accum))
+        assert all(len(b) == accum // world for b in blocks)
+    with pytest.raises(train.UsageError, match="not a multiple"):
+        train.rank_micros(6, 4, 0)
+
+
+def test_dist_info_from_torchrun_env():
+    assert train.DistInfo.from_env({}) == train.DistInfo(1, 0, 0)
+    assert train.DistInfo.from_env({"WORLD_SIZE": "1", "RANK": "0"}) == train.DistInfo(1, 0, 0)
+    assert train.DistInfo.from_env({"WORLD_SIZE": "4", "RANK": "6", "LOCAL_RANK": "2"}) == train.DistInfo(4, 6, 2)
+
+
+def test_main_rejects_accum_not_divisible_by_world(monkeypatch, capsys):
+    monkeypatch.setenv("WORLD_SIZE", "4")
+    monkeypatch.setenv("RANK", "0")
+    assert train.main(["--data", "d", "--accum", "6"]) == 1
+    assert "not a multiple" in capsys.readouterr().err
+
+
+def _mean_rank(rank, port, out):
+    import os
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    g = train._Group(train.DistInfo(2, rank, rank))
+    try:
+        m = g.mean([9.25, 8.75][rank])
+        if rank == 0:
+            np.save(out, np.array([m]))
+    finally:
+        g.close()
+
+
+def test_group_mean_over_gloo_ranks(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = str(tmp_path / "m.npy")
+    mp.spawn(_mean_rank, args=(port, out), nprocs=2, join=True)
+    assert np.load(out)[0] == np.float32(9.0)
