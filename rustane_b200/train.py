@@ -215,8 +215,10 @@ class _Group:
         import torch.distributed as tdist
         self.d, self.tdist = d, tdist
         self.owned = not tdist.is_initialized()
-        if self.owned:
-            tdist.init_process_group("gloo", rank=d.rank, world_size=d.world)
+        if self.owned:  # a rank that fails ends the others' next host collective within the timeout
+            import datetime
+            tdist.init_process_group("gloo", rank=d.rank, world_size=d.world,
+                                     timeout=datetime.timedelta(seconds=300))
 
     def join(self, kernels: CompiledKernels) -> None:
         uid = [CompiledKernels.nccl_unique_id() if self.d.rank == 0 else None]
