@@ -76,7 +76,7 @@ def workload_desc(cfg, name: str = "600m", batch: int = PER_GPU_BATCH) -> str:
 
 # --------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms during the timed region."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -91,7 +91,7 @@ class ClockSampler:
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -179,6 +179,104 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+# ------------------------------------------------------ the other configs
+EXTRA = (  # (key, workload, batch, timed steps, warm-up steps): BASELINE configs[2..4]
+    ("5b_train_b4", "5b", 4, 5, 3),
+    ("7b_fwd_b1", "7b", 1, 10, 3),
+    ("7b_fwd_b16", "7b", 16, 5, 3),
+    ("30b_fwd_b8", "30b", 8, 3, 3),
+)
+
+
+def measure_workload(wl: str, B: int, K: int, W: int, rank: int, world: int, local: int, dist) -> dict:
+    """One context of workload `wl` (data parallel when it trains, tensor parallel
+    otherwise), seeded device weights, two staged batches; W warm-up steps, then K
+    steps timed by CUDA events on the context stream (max over ranks), then three
+    profiled steps for the GEMM roofline.  The context is freed before returning."""
+    import torch
+    from rustane_b200 import CompiledKernels, TrainConfig, _lib
+
+    train = WORKLOADS[wl][1]
+    cfg = workload_cfg(wl)
+    L = _lib.lib()
+    k = CompiledKernels.compile(cfg, max_batch=B, device=local, forward_only=not train)
+    try:
+        if world > 1:
+            uid = [CompiledKernels.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            k.dist_init(world, rank, uid[0], _lib.RT_DIST_DATA_PARALLEL if train else _lib.RT_DIST_TENSOR_PARALLEL,
+                        timeout_ms=120000)
+        k.init_normal(seed=SEED_WEIGHTS, std=0.02)
+        rng = np.random.default_rng(1000 + (rank if train else 0))
+        for slot in range(2):
+            tok = rng.integers(0, cfg.vocab, B * cfg.seq).astype(np.uint32)
+            tgt = rng.integers(0, cfg.vocab, B * cfg.seq).astype(np.uint32)
+            k._check(L.rt_stage_batch(k.handle, slot, tok.ctypes.data_as(_lib.c_uint32_p),
+                                      tgt.ctypes.data_as(_lib.c_uint32_p), B))
+        c_tc = TrainConfig().to_c()
+        step = 0
+
+        def steps(n):
+            nonlocal step
+            for _ in range(n):
+                if train:
+                    k._check(L.rt_train_step_staged(k.handle, step % 2, step, ctypes.byref(c_tc), None))
+                else:
+                    k._check(L.rt_forward_staged(k.handle, step % 2, ctypes.c_float(0.0)))
+                step += 1
+
+        steps(W)
+        k._check(L.rt_sync(k.handle, None))
+        sp = ctypes.c_void_p()
+        k._check(L.rt_ctx_stream(k.handle, ctypes.byref(sp)))
+        stream = torch.cuda.ExternalStream(sp.value)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            ev0.record(stream)
+            steps(K)
+            k._check(L.rt_join(k.handle))
+            ev1.record(stream)
+            loss = ctypes.c_float()
+            k._check(L.rt_sync(k.handle, ctypes.byref(loss)))
+            torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if dist is not None:
+            t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        k.profile(True)
+        steps(3)
+        k._check(L.rt_sync(k.handle, None))
+        tm = k.timings()
+        k.profile(False)
+    finally:
+        k.close()
+    ms_step = ms / K
+    tokens = (world if train else 1) * B * cfg.seq
+    flops = (3.0 if train else 1.0) * cfg.flops_per_token_fwd() * B * cfg.seq / (1 if train else world)
+    pk = peaks()
+    gemm_tf = tm["gemm_flops"] / (tm["gemm_ms"] * 1e-3) / 1e12 if tm["gemm_ms"] > 0 else None
+    out = {"workload": workload_desc(cfg, wl, B), "parallelism": (f"dp{world}" if train else f"tp{world}"),
+           "ms_per_step": ms_step, "tok_s": tokens / (ms_step * 1e-3),
+           "step_tflops_per_gpu": flops / (ms_step * 1e-3) / 1e12,
+           "tc_util_vs_spec_2250": flops / (ms_step * 1e-3) / 1e12 / SPEC_BF16_TFLOPS,
+           "gemm_roofline": {"achieved": gemm_tf, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                             "frac": gemm_tf / pk["bf16_sustained"] if gemm_tf else None,
+                             "peak_source": pk["source"] + " sustained bf16"},
+           "steps": K, "warmup": W, "loss_last": loss.value, "clocks": clocks.summary()}
+    if not train:
+        out["fwd_ms"] = ms_step
+    if train:
+        out["step_breakdown_ms"] = {"fwd": tm["fwd_ms"], "bwd": tm["bwd_ms"], "norm_adam": tm["opt_ms"]}
+    if wl in PUBLISHED:
+        out["vs_published"] = out["tok_s"] / PUBLISHED[wl][0]
+        out["published_basis"] = PUBLISHED[wl][1] + ", Apple M4 Max"
+    return out
+
+
 # ------------------------------------------------------------- our arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -189,6 +287,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="600m", choices=list(WORKLOADS))
     ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the 5B / 7B / 30B lines that follow the 600M measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -363,6 +463,14 @@ def main() -> None:
                                   "sample": f"{len(times)} train step(s) of 1 x {cfg.seq} tokens, 600M config",
                                   "blas": blas}
     k.close()
+    if wl == "600m" and not args.no_extra:
+        extra = {}
+        for key, ewl, eb, ek, ew in EXTRA:
+            try:
+                extra[key] = measure_workload(ewl, eb, ek, ew, rank, world, local, dist)
+            except Exception as e:  # noqa: BLE001 -- reported in the line, the headline stands
+                extra[key] = {"error": f"{type(e).__name__}: {e}"}
+        result["workloads"] = extra
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -5,8 +5,8 @@
  * This library is the `cuda-bridge` that replaces the `ane` crate surface the
  * engine crate binds today (crates/ane-bridge/src/lib.rs:1-9; graph build +
  * compile + eval at crates/engine/src/layer.rs:237-275, :600-602), the MIL
- * graph builders (crates/engine/src/kernels/*.rs) and the Accelerate CPU ops
- * (crates/engine/src/cpu/*.rs).  Each entry point below names the reference
+ * graph builders (the files of crates/engine/src/kernels/) and the Accelerate
+ * CPU ops (crates/engine/src/cpu/).  Each entry point below names the reference
  * interface it replaces.
  *
  * Conventions
@@ -160,6 +160,15 @@ RT_API int rt_backward(rt_ctx* ctx, float softcap, float loss_scale);
 RT_API int rt_grads_zero(rt_ctx* ctx);
 /* Global L2 norm of all gradients (grad_norm, full_model.rs:598-624). */
 RT_API int rt_grad_norm(rt_ctx* ctx, float* norm_out);
+/* The raw global gradient norm the last rt_train_step / rt_train_step_staged
+ * (or rt_grad_norm) computed on the device, without recomputing it: the value
+ * the training loop logs as gnorm / (accum * loss_scale) (bin/train.rs:252-290
+ * calls grad_norm, full_model.rs:598-624, after each step).  Under data
+ * parallelism it is the norm of the gradients summed over the ranks, so a
+ * sharded step needs no gather to report it.  RT_ERR_STATE when no norm was
+ * computed since the context was created or a single-layer call reused the
+ * slot. */
+RT_API int rt_last_grad_norm(rt_ctx* ctx, float* norm_out);
 /* clip_grads (full_model.rs:627-645). */
 RT_API int rt_clip_grads(rt_ctx* ctx, float max_norm);
 /* AdamW with the reference's learning-rate groups (update_weights,
@@ -253,6 +262,14 @@ RT_API int rt_checkpoint_read(const char* path, const rt_model_config* cfg, uint
 
 /* NCCL unique id (128 bytes) for rank 0 to broadcast to the other ranks. */
 RT_API int rt_nccl_unique_id(uint8_t* out128);
+/* The tensor-parallel partition rt_dist_init applies (host only, no device):
+ * rank `rank` of `world` owns heads [head0, head0 + heads_loc) and hidden
+ * columns [hid0, hid0 + hid_loc).  The first heads % world ranks take one
+ * extra head; the hidden columns are split likewise in 64-column units (52
+ * heads over 8 ranks: 7,7,7,7,6,6,6,6).  Replaces the all-heads layout of
+ * layer::forward_into (layer.rs:552-680), which has no sharded form. */
+RT_API int rt_tp_shard(int heads, int hidden, int world, int rank, int* head0, int* heads_loc, int* hid0,
+                       int* hid_loc);
 /* Join a communicator of `world` ranks (one process per GPU).  mode:
  * RT_DIST_DATA_PARALLEL or RT_DIST_TENSOR_PARALLEL.  Collectives that do not
  * finish within timeout_ms abort the communicator and return RT_ERR_NCCL.

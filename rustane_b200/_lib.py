@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "rt_backward": (c_int, [c_void_p, c_float, c_float]),
     "rt_grads_zero": (c_int, [c_void_p]),
     "rt_grad_norm": (c_int, [c_void_p, c_float_p]),
+    "rt_last_grad_norm": (c_int, [c_void_p, c_float_p]),
     "rt_clip_grads": (c_int, [c_void_p, c_float]),
     "rt_update_weights": (c_int, [c_void_p, c_uint32, c_float, P_TC, c_float]),
     "rt_learning_rate": (c_float, [c_uint32, P_TC]),
@@ -85,6 +86,8 @@ SIGNATURES: dict[str, tuple] = {
     "rt_last_h2d_bytes": (c_int, [c_void_p, ctypes.POINTER(c_int64)]),
     "rt_nccl_unique_id": (c_int, [c_uint8_p]),
     "rt_dist_init": (c_int, [c_void_p, c_int, c_int, c_uint8_p, c_int, c_int]),
+    "rt_tp_shard": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                            ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "rt_grad_allreduce": (c_int, [c_void_p]),
     "rt_join": (c_int, [c_void_p]),
     "rt_tokens_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_void_p)]),

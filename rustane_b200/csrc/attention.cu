@@ -413,8 +413,6 @@ __global__ void __launch_bounds__(BWD_NT, 2)
   store_tile<BWD_B, BWD_NT>(sQ, dqkv + (tok0 + q0) * lddq + h * HD, lddq, tid);
 }
 
-bool g_attr_done = false;
-
 }  // namespace
 
 int attn_bwd_rowsum(const AttnArgs& a, cudaStream_t s) {
@@ -428,11 +426,9 @@ int attn_bwd_rowsum(const AttnArgs& a, cudaStream_t s) {
 
 int attn_backward(const AttnArgs& a, cudaStream_t s) {
   if (a.S % 128 != 0 || a.hd != HD || a.D != a.heads * HD) return -1;
-  if (!g_attr_done) {
-    cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
-    g_attr_done = true;
-  }
+  cudaError_t attr = smem_limit_once(reinterpret_cast<const void*>(attn_bwd_dkdv_kernel), BWD_SMEM);
+  if (attr == cudaSuccess) attr = smem_limit_once(reinterpret_cast<const void*>(attn_bwd_dq_kernel), BWD_SMEM);
+  if (attr != cudaSuccess) return attr;
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   const float scale_log2 = scale * 1.4426950408889634f;
   const int rc = attn_bwd_rowsum(a, s);

@@ -600,10 +600,8 @@ int attn_backward_tc(const AttnArgs& a, cudaStream_t s) {
       !make_tmap_bf16(&tm_ds2, a.ds_scratch, kSub, ds_rows, kSub, 64, 2 * kKeys) ||
       !make_tmap_bf16(&tm_out, a.dqkv, 3 * static_cast<uint64_t>(a.D), M, a.lddq, 64, kKeys))
     return -3;
-  static const cudaError_t attr1 =
-      cudaFuncSetAttribute(attn_bwd_kv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KvSmem::BYTES);
-  static const cudaError_t attr2 =
-      cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem::BYTES);
+  const cudaError_t attr1 = smem_limit_once(reinterpret_cast<const void*>(attn_bwd_kv_tc_kernel), KvSmem::BYTES);
+  const cudaError_t attr2 = smem_limit_once(reinterpret_cast<const void*>(attn_bwd_dq_tc_kernel), DqSmem::BYTES);
   if (attr1 != cudaSuccess) return attr1;
   if (attr2 != cudaSuccess) return attr2;
   int rc = attn_bwd_rowsum(a, s);

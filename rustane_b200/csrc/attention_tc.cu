@@ -347,8 +347,7 @@ int attn_forward(const AttnArgs& a, cudaStream_t s) {
   if (!make_tmap_bf16(&tm, a.qkv, static_cast<uint64_t>(3) * a.D, M, a.ldq, 64, kBlk) ||
       !make_tmap_bf16(&tm_out, a.out, static_cast<uint64_t>(a.D), M, a.ldo, 64, kBlk))
     return -3;
-  static const cudaError_t attr =
-      cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdSmem::BYTES);
+  const cudaError_t attr = smem_limit_once(reinterpret_cast<const void*>(attn_fwd_tc_kernel), FwdSmem::BYTES);
   if (attr != cudaSuccess) return attr;
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kHd));
   dim3 grid(a.heads, a.batch, a.S / kBlk);

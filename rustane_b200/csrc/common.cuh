@@ -282,4 +282,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool a_mn, b
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// Raises kernel `fn`'s dynamic shared-memory limit to `bytes` on the CURRENT
+// device, once per (kernel, device).  The attribute belongs to the device that
+// is current when it is set, so a process that drives several GPUs (one
+// context per device) needs it on each; the table is guarded by a mutex, so
+// first calls from several threads are safe.  Defined in runtime.cu.
+cudaError_t smem_limit_once(const void* fn, int bytes);
+
 }  // namespace rt

@@ -726,8 +726,7 @@ template <int NV2, int STAGES>
 int launch_norm_pipe(const float* dy, const float* x, const float* gamma, const float* rms_inv, const float* resid,
                      float* dx, __nv_bfloat16* dx_bf16, float bf16_scale, float* part, int M, int D, cudaStream_t s) {
   constexpr int smem = STAGES * 2 * kGroupRows * 64 * NV2 * 16;
-  static const cudaError_t attr =
-      cudaFuncSetAttribute(rmsnorm_bwd_pipe_kernel<NV2, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const cudaError_t attr = smem_limit_once(reinterpret_cast<const void*>(rmsnorm_bwd_pipe_kernel<NV2, STAGES>), smem);
   if (attr != cudaSuccess) return attr;
   rmsnorm_bwd_pipe_kernel<NV2, STAGES><<<norm_ctas(M), 256, smem, s>>>(dy, x, gamma, rms_inv, resid, dx, dx_bf16,
                                                                        bf16_scale, part, M, D);

@@ -757,8 +757,8 @@ bool make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer,
 template <int BN, bool A_MN, bool B_MN, int EPI>
 int launch_inst(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid, cudaStream_t s) {
   using C = GemmCfg<BN>;
-  static const cudaError_t attr = cudaFuncSetAttribute(gemm_tc_kernel<BN, A_MN, B_MN, EPI>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  const cudaError_t attr =
+      smem_limit_once(reinterpret_cast<const void*>(gemm_tc_kernel<BN, A_MN, B_MN, EPI>), C::SMEM_BYTES);
   if (attr != cudaSuccess) return attr;
   gemm_tc_kernel<BN, A_MN, B_MN, EPI><<<grid, kThreads, C::SMEM_BYTES, s>>>(ta, tb, kp);
   return cudaGetLastError();
@@ -767,8 +767,8 @@ int launch_inst(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
 template <int BN, bool A_MN, bool B_MN, int EPI>
 int launch_inst2(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid, cudaStream_t s) {
   using C = Gemm2Cfg<BN>;
-  static const cudaError_t attr = cudaFuncSetAttribute(gemm_tc2_kernel<BN, A_MN, B_MN, EPI>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  const cudaError_t attr =
+      smem_limit_once(reinterpret_cast<const void*>(gemm_tc2_kernel<BN, A_MN, B_MN, EPI>), C::SMEM_BYTES);
   if (attr != cudaSuccess) return attr;
   gemm_tc2_kernel<BN, A_MN, B_MN, EPI><<<grid, kThreads, C::SMEM_BYTES, s>>>(ta, tb, kp);
   return cudaGetLastError();

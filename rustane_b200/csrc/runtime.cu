@@ -16,7 +16,10 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <mutex>
+#include <set>
 #include <thread>
+#include <utility>
 
 #include "attention.h"
 #include "common.cuh"
@@ -25,6 +28,22 @@
 #include "runtime.h"
 
 using rt::bf16;
+
+// ============================================ per-device kernel attributes
+namespace rt {
+cudaError_t smem_limit_once(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;  // (kernel, device)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev})) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert({fn, dev});
+  return e;
+}
+}  // namespace rt
 
 // ================================================================ NCCL (dlopen)
 namespace rt {
@@ -50,6 +69,8 @@ struct NcclState {
 static NcclApi* nccl_api() {
   static NcclApi api;
   static bool tried = false;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
   if (tried) return api.handle ? &api : nullptr;
   tried = true;
   const char* env = getenv("RUSTANE_NCCL_LIB");
@@ -1429,7 +1450,20 @@ RT_API int rt_grad_norm(rt_ctx* c, float* norm_out) {
   RT_OTHER(2, rt::sumsq_norm(c->grads, c->n_params, c->norm_partials, c->d_norm, c->stream), "grad norm");
   RT_CUDA(cudaMemcpyAsync(c->h_loss + 1, c->d_norm, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "norm d2h");
   if ((rc = wait_stream(c))) return rc;
+  c->norm_valid = true;
   if (norm_out) *norm_out = c->h_loss[1];
+  return RT_OK;
+}
+
+RT_API int rt_last_grad_norm(rt_ctx* c, float* norm_out) {
+  int rc;
+  if ((rc = check_train(c))) return rc;
+  if (!norm_out) return set_err(c, RT_ERR_ARG, "null argument");
+  if (!c->norm_valid) return set_err(c, RT_ERR_STATE, "no gradient norm computed yet");
+  cudaSetDevice(c->device);
+  RT_CUDA(cudaMemcpyAsync(c->h_loss + 1, c->d_norm, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "norm d2h");
+  if ((rc = wait_stream(c))) return rc;
+  *norm_out = c->h_loss[1];
   return RT_OK;
 }
 
@@ -1557,6 +1591,7 @@ RT_API int rt_layer_train_step(rt_ctx* c, int layer, const float* x, int batch, 
   if ((rc = layer_forward_host(c, layer, x, batch))) return rc;
   const int64_t n = int64_t(batch) * c->cfg.seq * c->cfg.dim;
   // loss = mean(y^2) through the fixed-order L2 norm; dy = 2 y / n
+  c->norm_valid = false;  // d_norm now holds the layer loss
   RT_OTHER(2, rt::sumsq_norm(c->x_out, n, c->norm_partials, c->d_norm, c->stream), "layer loss");
   RT_OTHER(1, rt::scale_f32(c->x_out, c->dy_a, n, 2.0f / static_cast<float>(n), c->stream), "dy");
   // grads.zero_out() of this layer: its weight gradients are overwritten (beta = 0)
@@ -1618,6 +1653,7 @@ static int train_step_device(rt_ctx* c, const rt::TokenBatch& tb, uint32_t step,
   } else {
     RT_OTHER(1, rt::sumsq_finish(c->norm_partials, nparts, c->d_norm, c->stream), "grad norm");
   }
+  c->norm_valid = true;
   const float gsc = 1.0f / (static_cast<float>(batch) * static_cast<float>(c->world) * tc->loss_scale);
   const float lr = rt_learning_rate(step, tc);
   if (!shard) {
@@ -1747,6 +1783,27 @@ RT_API int rt_nccl_unique_id(uint8_t* out128) {
   return RT_OK;
 }
 
+RT_API int rt_tp_shard(int heads, int hidden, int world, int rank, int* head0, int* heads_loc, int* hid0,
+                       int* hid_loc) {
+  if (!head0 || !heads_loc || !hid0 || !hid_loc) return RT_ERR_ARG;
+  if (world < 1 || rank < 0 || rank >= world || heads < world) return RT_ERR_SHAPE;
+  if (world == 1) {
+    *head0 = *hid0 = 0;
+    *heads_loc = heads;
+    *hid_loc = hidden;
+    return RT_OK;
+  }
+  if (hidden % 64 != 0 || hidden / 64 < world) return RT_ERR_SHAPE;
+  // heads: the first heads % world ranks take one extra; hidden columns likewise in 64-column units
+  const int units = hidden / 64;
+  const int hb = heads / world, hr = heads % world, ub = units / world, ur = units % world;
+  *heads_loc = hb + (rank < hr ? 1 : 0);
+  *head0 = rank * hb + std::min(rank, hr);
+  *hid_loc = 64 * (ub + (rank < ur ? 1 : 0));
+  *hid0 = 64 * (rank * ub + std::min(rank, ur));
+  return RT_OK;
+}
+
 RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms) {
   if (!c || world <= 0 || rank < 0 || rank >= world) return RT_ERR_ARG;
   if (mode != RT_DIST_DATA_PARALLEL && mode != RT_DIST_TENSOR_PARALLEL) return RT_ERR_ARG;
@@ -1755,7 +1812,8 @@ RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id
   if (mode == RT_DIST_TENSOR_PARALLEL) {
     if (!forward_only(c)) return set_err(c, RT_ERR_STATE, "tensor parallelism needs a forward-only context");
     if (c->weights_set) return set_err(c, RT_ERR_STATE, "call rt_dist_init before uploading or initialising weights");
-    if (world > nh || world > units) return set_err(c, RT_ERR_SHAPE, "more tensor-parallel ranks than heads");
+    if (world > nh || world > units || (world > 1 && c->cfg.hidden % 64 != 0))
+      return set_err(c, RT_ERR_SHAPE, "more tensor-parallel ranks than heads or 64-column hidden units");
   }
   // join the communicator before changing the context, so that a failed join leaves it as it was
   rt::NcclApi* api = nullptr;
@@ -1773,14 +1831,9 @@ RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id
     c->nccl->comm = comm;
   }
   if (mode == RT_DIST_TENSOR_PARALLEL) {
-    // shard heads (uneven split allowed) and hidden columns (64-column units) over the ranks
-    const int hb = nh / world, hr = nh % world, ub = units / world, ur = units % world;
     free_shard_buffers(c);
     c->tp = world > 1;
-    c->heads_loc = hb + (rank < hr ? 1 : 0);
-    c->head0 = rank * hb + std::min(rank, hr);
-    c->hid_loc = 64 * (ub + (rank < ur ? 1 : 0));
-    c->hid0 = 64 * (rank * ub + std::min(rank, ur));
+    rt_tp_shard(nh, c->cfg.hidden, world, rank, &c->head0, &c->heads_loc, &c->hid0, &c->hid_loc);
     layout_bf16(c);
     if (!alloc_shard_buffers(c)) return set_err(c, RT_ERR_OOM, "tensor-parallel shard allocation");
   }

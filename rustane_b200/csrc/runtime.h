@@ -89,6 +89,7 @@ struct rt_ctx {
   float* row_lse = nullptr;
   float* d_loss = nullptr;  // [1]
   float* d_norm = nullptr;  // [1]
+  bool norm_valid = false;  // d_norm holds the last computed gradient norm
   float* norm_partials = nullptr;
 
   // backward scratch

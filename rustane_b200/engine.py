@@ -193,6 +193,12 @@ class CompiledKernels:
         self._check(lib().rt_grad_norm(self.handle, ctypes.byref(n)))
         return n.value
 
+    def last_grad_norm(self) -> float:
+        """The raw gradient norm the last train step computed on the device (no recompute, no gather)."""
+        n = ctypes.c_float()
+        self._check(lib().rt_last_grad_norm(self.handle, ctypes.byref(n)))
+        return n.value
+
     def clip_grads(self, max_norm: float) -> None:
         self._check(lib().rt_clip_grads(self.handle, max_norm))
 
@@ -272,6 +278,14 @@ def learning_rate(step: int, tc: TrainConfig) -> float:
     """full_model.rs:334-342."""
     c_tc = tc.to_c()
     return lib().rt_learning_rate(step, ctypes.byref(c_tc))
+
+
+def tp_shard(heads: int, hidden: int, world: int, rank: int) -> tuple[int, int, int, int]:
+    """The tensor-parallel partition of the library (rt_tp_shard): this rank's
+    (head0, heads_loc, hid0, hid_loc)."""
+    v = [ctypes.c_int() for _ in range(4)]
+    check(lib().rt_tp_shard(heads, hidden, world, rank, *[ctypes.byref(x) for x in v]))
+    return tuple(x.value for x in v)
 
 
 def lcg_random_vec(n: int, scale: float) -> np.ndarray:

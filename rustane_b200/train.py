@@ -322,6 +322,19 @@ def _run(a: Args, tc: TrainConfig, micros: range, dist: DistInfo, group, out) ->
     max_batch = max(len(micros), min(max(a.val_steps, 1), 32))
     device = dist.local_rank if group is not None else a.device
     kernels = CompiledKernels.compile(cfg, max_batch=max_batch, device=device)
+    try:
+        return _train(a, cfg, tc, micros, dist, group, out, kernels, train_data, val_data, token_bytes, t0)
+    finally:
+        # a failing rank (non-finite loss, a communicator timeout) releases its
+        # context and communicator at once instead of holding the other ranks
+        kernels.close()
+        train_data.close()
+        if val_data is not None:
+            val_data.close()
+
+
+def _train(a: Args, cfg, tc: TrainConfig, micros: range, dist: DistInfo, group, out, kernels, train_data, val_data,
+           token_bytes, t0: float) -> RunResult:
     if group is not None:
         group.join(kernels)
         out(f"  data parallel: {dist.world} ranks x {len(micros)} microbatches")
@@ -367,7 +380,7 @@ def _run(a: Args, tc: TrainConfig, micros: range, dist: DistInfo, group, out) ->
         avg_loss = kernels.train_step(tok, tgt, step, tc)
         if group is not None:
             avg_loss = group.mean(avg_loss)
-        gnorm = float(np.float32(kernels.grad_norm()) * gsc)
+        gnorm = float(np.float32(kernels.last_grad_norm()) * gsc)
         lr = learning_rate(step, tc)
         step_time = time.perf_counter() - step_t0
         elapsed = time.perf_counter() - train_start
@@ -400,10 +413,6 @@ def _run(a: Args, tc: TrainConfig, micros: range, dist: DistInfo, group, out) ->
     out(f"  time: {res.seconds:.1f}s ({res.seconds / 60.0:.1f} min)")
     if res.best_bpb < float("inf"):
         out(f"  best val_bpb: {res.best_bpb:.4f}")
-    kernels.close()
-    train_data.close()
-    if val_data is not None:
-        val_data.close()
     return res
 
 

@@ -1,0 +1,177 @@
+"""Parity on the configurations bench.py measures, through bench.py's own path.
+
+The weights are the bench's (``rt_weights_init_normal`` seed 1234, std 0.02,
+generated on the device), downloaded into the CPU oracle; the tokens are the
+bench's first staged batch (uniform ids, numpy seed 1000, tokens then
+targets); the GPU runs ``rt_stage_batch`` then ``rt_forward_staged`` /
+``rt_train_step_staged`` exactly as ``bench.py`` times them, so the GEMM tile
+variants, raster bands and attention grids are the ones the bench line uses
+(they depend on the token count M = batch x 512 and the widths, not on the
+depth, which is reduced here to keep the fp32 oracle within seconds).
+
+Reference math: full_model.rs:187-331 (forward / backward), :661-714
+(train_step), :490-593 (update_weights).  Tolerances:
+loss within 2e-3 absolute; logits and every gradient tensor within 2e-2 of
+max|oracle| (normwise max relative error).  The AdamW update is checked in
+two parts: (1) the oracle's update_weights applied to the GPU's own gradients
+(same clip rule and learning-rate groups) must give the GPU's new weights
+within four fp32 ulps of each weight plus four ulps of its update (the device
+fuses w - lr * u into one multiply-add, so the update's own rounding shows in
+weights near zero, and it sums the norm in another order); (2) the loss of the next forward, GPU
+weights after the step against oracle weights after the oracle's own step,
+within the loss tolerance.  A per-entry comparison of the two independent
+updates is not meaningful: the first AdamW step moves each entry by
+lr * g / (|g| + eps), so entries whose gradient is near zero (or near eps) take
+steps of either sign within the gradient tolerance.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import pyoracle as po  # noqa: E402
+from rustane_b200 import CompiledKernels, ModelConfig, TrainConfig, _lib  # noqa: E402
+from rustane_b200.tensors import ModelOptState, ModelTensors  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+LOSS_TOL = 2e-3
+REL_TOL = 2e-2
+SEED_WEIGHTS, SEED_TOKENS = 1234, 1000  # bench.py's seeds
+
+
+def nrel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def bench_batch(cfg, batch):
+    """bench.py's slot 0: tokens then targets from default_rng(1000)."""
+    rng = np.random.default_rng(SEED_TOKENS)
+    tok = rng.integers(0, cfg.vocab, batch * cfg.seq).astype(np.uint32)
+    tgt = rng.integers(0, cfg.vocab, batch * cfg.seq).astype(np.uint32)
+    return tok, tgt
+
+
+def stage(k, tok, tgt, batch, slot=0):
+    L = _lib.lib()
+    k._check(L.rt_stage_batch(k.handle, slot, tok.ctypes.data_as(_lib.c_uint32_p),
+                              tgt.ctypes.data_as(_lib.c_uint32_p), batch))
+
+
+def forward_staged(k, slot=0):
+    L = _lib.lib()
+    k._check(L.rt_forward_staged(k.handle, slot, ctypes.c_float(0.0)))
+    loss = ctypes.c_float()
+    k._check(L.rt_sync(k.handle, ctypes.byref(loss)))
+    return loss.value
+
+
+def device_weights(cfg, batch):
+    """The bench's device-initialised weights, read back through a training context."""
+    k = CompiledKernels.compile(cfg, max_batch=batch)
+    k.init_normal(seed=SEED_WEIGHTS, std=0.02)
+    w = k.download_weights()
+    return k, w
+
+
+def check_grads(g_gpu: ModelTensors, g_ref: ModelTensors):
+    worst = {}
+    for (name, a), (_, b) in zip(g_gpu.tensors(), g_ref.tensors()):
+        if np.max(np.abs(b)) == 0:
+            assert np.max(np.abs(a)) == 0, name
+            continue
+        worst[name] = nrel(a, b)
+    bad = {n: v for n, v in worst.items() if v > REL_TOL}
+    assert not bad, bad
+    return worst
+
+
+TRAIN_CASES = {
+    # id: (config, batch) -- widths of BASELINE configs[1] / [2] at the bench's per-GPU batch
+    "600m-width-2layers-b8": (ModelConfig.custom(1536, 4096, 12, 2), 8),
+    "600m-full-depth-b1": (ModelConfig.c600m(), 1),
+    "5b-width-1layer-b4": (ModelConfig.custom(2560, 6912, 20, 1), 4),
+}
+
+
+@pytest.mark.parametrize("case", list(TRAIN_CASES))
+def test_train_step_parity_bench_path(case):
+    cfg, batch = TRAIN_CASES[case]
+    k, w0 = device_weights(cfg, batch)
+    tok, tgt = bench_batch(cfg, batch)
+    stage(k, tok, tgt, batch)
+
+    o = po.Oracle(cfg, batch)
+    # forward: loss and logits
+    loss_fwd = forward_staged(k)
+    loss_ref, logits_ref, _ = o.forward(w0, tok, tgt, want_logits=True)
+    assert abs(loss_fwd - loss_ref) < LOSS_TOL, (loss_fwd, loss_ref)
+    assert nrel(k_logits(k, cfg, batch), logits_ref) < REL_TOL
+    del logits_ref
+
+    # one train step (forward, backward, grad norm + clip, AdamW) as bench.py runs it
+    tc = TrainConfig()
+    c_tc = tc.to_c()
+    loss = ctypes.c_float()
+    k._check(_lib.lib().rt_train_step_staged(k.handle, 0, 0, ctypes.byref(c_tc), ctypes.byref(loss)))
+    w_ref, g_ref, opt_ref = w0.copy(), ModelTensors.zeros(cfg), ModelOptState.zeros(cfg)
+    loss_step_ref, _ = o.train_step(w_ref, g_ref, opt_ref, tok, tgt, 0, po.default_train_config())
+    assert abs(loss.value - loss_step_ref) < LOSS_TOL, (loss.value, loss_step_ref)
+    g_gpu = k.download_grads()
+    check_grads(g_gpu, g_ref)
+    del g_ref
+
+    # (1) AdamW on the GPU's gradients: full_model.rs:696-704 (clip rule), :490-593 (groups)
+    otc = po.default_train_config()
+    gsc = np.float32(1.0) / (np.float32(batch) * np.float32(otc.loss_scale))
+    raw = o.grad_norm(g_gpu)
+    combined = otc.grad_clip / raw if raw * gsc > otc.grad_clip else gsc
+    w_chk = w0.copy()
+    o.update_weights(w_chk, g_gpu, ModelOptState.zeros(cfg), 1, po.learning_rate(0, otc), otc, float(combined))
+    del g_gpu
+    w1 = k.download_weights()
+    for (name, a), (_, b), (_, a0) in zip(w1.tensors(), w_chk.tensors(), w0.tensors()):
+        err = np.abs(a.astype(np.float64) - b)
+        bound = 4 * np.spacing(np.abs(b)).astype(np.float64) + 4 * np.spacing(np.abs(b - a0)).astype(np.float64)
+        assert np.all(err <= bound), (name, int(np.sum(err > bound)), float(err.max()))
+    del w_chk
+
+    # (2) the next forward's loss after each side's own step
+    loss2 = forward_staged(k)
+    loss2_ref, _, _ = o.forward(w_ref, tok, tgt)
+    assert abs(loss2 - loss2_ref) < LOSS_TOL, (loss2, loss2_ref)
+    k.close()
+
+
+def k_logits(k, cfg, batch):
+    out = np.empty((batch * cfg.seq, cfg.vocab), np.float32)
+    k._check(_lib.lib().rt_logits_download(k.handle, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+    return out
+
+
+FWD_CASES = {
+    # forward-only contexts (bf16 weights) at the widths of BASELINE configs[3] / [4]
+    "7b-width-2layers-b1": (ModelConfig.custom(4096, 11008, 32, 2), 1),
+    "7b-width-1layer-b16": (ModelConfig.custom(4096, 11008, 32, 1), 16),
+    "30b-width-1layer-b1": (ModelConfig.custom(6656, 17920, 52, 1), 1),
+}
+
+
+@pytest.mark.parametrize("case", list(FWD_CASES))
+def test_forward_only_parity_bench_path(case):
+    cfg, batch = FWD_CASES[case]
+    kt, w = device_weights(cfg, 1)
+    kt.close()  # the forward-only context generates the same weights (by global index) in bf16
+    k = CompiledKernels.compile(cfg, max_batch=batch, forward_only=True)
+    k.init_normal(seed=SEED_WEIGHTS, std=0.02)
+    tok, tgt = bench_batch(cfg, batch)
+    stage(k, tok, tgt, batch)
+    loss = forward_staged(k)
+    o = po.Oracle(cfg, batch)
+    loss_ref, logits_ref, _ = o.forward(w, tok, tgt, want_logits=True)
+    assert abs(loss - loss_ref) < LOSS_TOL, (loss, loss_ref)
+    assert nrel(k_logits(k, cfg, batch), logits_ref) < REL_TOL
+    k.close()
