@@ -79,9 +79,11 @@ enum KvBar : int {
 
 struct DqSmem {
   static constexpr int STAGE = 2 * kKvTile;  // dS (two 64-query tiles of 128 keys) + K_j
-  static constexpr int BAR = kDqStages * STAGE;
+  static constexpr int OUT = kDqStages * STAGE;  // dQ staging for the TMA store
+  static constexpr int BAR = OUT + kKvTile;
   static constexpr int BYTES = BAR + 128 + 1024;
 };
+static_assert(DqSmem::BYTES <= 232448, "dq kernel shared memory");
 
 // ------------------------------------------------------------------ dK, dV
 __global__ void __launch_bounds__(kKvThreads, 1)
@@ -308,12 +310,15 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     for (int t = 0; ok && t < n; ++t) {
       const uint32_t ph = t & 1;
       const int q0 = (j + t) * kKeys + hh * 64;  // first query of this thread's 64 columns
-      // lse2 and rowsum of this warp's 64 queries: lane e holds queries q0 + e and q0 + 32 + e (from L2)
+      // lse2 and rowsum of this warp's 64 queries: lane e holds queries q0 + e and q0 + 32 + e (from L2,
+      // loaded while the MMAs run); every lane needs all 64, passed around by shuffles
       const float l0 = __ldg(lse2 + stat0 + q0 + lane), l1 = __ldg(lse2 + stat0 + q0 + 32 + lane);
       const float d0 = __ldg(rowsum + stat0 + q0 + lane), d1 = __ldg(rowsum + stat0 + q0 + 32 + lane);
       if (!wait(&bar[kSFull], ph)) break;
       tc_fence_after();
-      float p[64];
+      // P^T = exp2(S^T * scale - lse) on column pairs (packed fp32x2); kept as pairs for dS^T
+      uint64_t p2[32];
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
@@ -321,12 +326,25 @@ __global__ void __launch_bounds__(kKvThreads, 1)
         tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float pe = exp2f(__uint_as_float(v[e]) * scale_log2 - __shfl_sync(0xffffffffu, c ? l1 : l0, e));
-          p[c * 32 + e] = q0 + c * 32 + e >= kpos ? pe : 0.f;  // causal: query before key -> 0
-        }
+        for (int u = 0; u < 8; ++u) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(p[c * 32 + 2 * e], p[c * 32 + 2 * e + 1]);
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int e = 4 * u + 2 * h2;
+            const float la = __shfl_sync(0xffffffffu, c ? l1 : l0, e);
+            const float lb = __shfl_sync(0xffffffffu, c ? l1 : l0, e + 1);
+            float x0, x1;
+            f2_unpack(f2_sub(f2_mul(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2), f2_pack(la, lb)),
+                      x0, x1);
+            float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+            if (t == 0) {  // the diagonal block: a query before the key -> 0 (causal)
+              const int qa = q0 + c * 32 + e;
+              p0 = qa >= kpos ? p0 : 0.f;
+              p1 = qa + 1 >= kpos ? p1 : 0.f;
+            }
+            p2[c * 16 + e / 2] = f2_pack(p0, p1);
+            pk[e / 2] = pack_bf16x2(p0, p1);
+          }
+        }
         // P^T in bf16 pairs over this thread's own S^T columns (chunk 0, already read)
         tmem_st16(tmem + kColS + lane_off + hh * 64 + c * 16, pk);
       }
@@ -336,18 +354,25 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       if (lane == 0) mbar_arrive(&bar[kPFull]);
       if (!wait(&bar[kDpFull], ph)) break;
       tc_fence_after();
-      uint32_t dk[32];  // dS^T of the 64 columns, bf16 pairs
+      uint32_t dk[32];  // dS^T = P^T * (dP^T - rowsum) of the 64 columns, bf16 pairs
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
         tmem_ld32(tmem + kColDp + lane_off + hh * 64 + c * 32, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float x0 = p[c * 32 + e] * (__uint_as_float(v[e]) - __shfl_sync(0xffffffffu, c ? d1 : d0, e));
-          const float x1 =
-              p[c * 32 + e + 1] * (__uint_as_float(v[e + 1]) - __shfl_sync(0xffffffffu, c ? d1 : d0, e + 1));
-          dk[c * 16 + e / 2] = pack_bf16x2(x0, x1);
+        for (int u = 0; u < 8; ++u) {
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int e = 4 * u + 2 * h2;
+            const float da = __shfl_sync(0xffffffffu, c ? d1 : d0, e);
+            const float db = __shfl_sync(0xffffffffu, c ? d1 : d0, e + 1);
+            const uint64_t ds = f2_mul(p2[c * 16 + e / 2],
+                                       f2_sub(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), f2_pack(da, db)));
+            float x0, x1;
+            f2_unpack(ds, x0, x1);
+            dk[c * 16 + e / 2] = pack_bf16x2(x0, x1);
+          }
         }
       }
       tc_fence_before();
@@ -424,34 +449,44 @@ __global__ void __launch_bounds__(kKvThreads, 1)
 }
 
 // ---------------------------------------------------------------------- dQ
+// Persistent: one CTA per SM walks the (sequence, head, 128-query block) items,
+// heaviest first, CTA c taking items c, 2P-1-c, 2P+c, ...; the dS / K ring runs on
+// across items and the TMEM accumulator is double-buffered, so one item's
+// epilogue overlaps the next item's MMAs.
+__device__ __forceinline__ int dq_item(int c, int P, int t) {
+  return (t >> 1) * 2 * P + ((t & 1) ? 2 * P - 1 - c : c);
+}
+
 __global__ void __launch_bounds__(kDqThreads, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_ds2,
-                          const __grid_constant__ CUtensorMap tm_out, int D, int S, int nh, float scale,
+                          const __grid_constant__ CUtensorMap tm_out, int D, int S, int nh, int batch, float scale,
                           const float* __restrict__ cosb, const float* __restrict__ sinb, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DqSmem::BAR);  // full[3], empty[3], acc, drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2 * kDqStages + 2);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DqSmem::BAR);
+  uint64_t* full = bar;                    // [kDqStages]
+  uint64_t* empty = bar + kDqStages;       // [kDqStages]
+  uint64_t* acc_full = bar + 2 * kDqStages;  // [2] accumulator buffer complete
+  uint64_t* acc_free = acc_full + 2;         // [2] the epilogue has read it
+  uint64_t* drain = acc_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* full = bar;
-  uint64_t* empty = bar + kDqStages;
-  uint64_t* acc = bar + 2 * kDqStages;
-  uint64_t* drain = acc + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = gridDim.z - 1 - blockIdx.z;  // heaviest query blocks first
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int nb = qb + 1;  // key blocks 0 .. qb
   const int nsub = S / kSub, nkb = S / kKeys;
-  const int tok0 = b * S;
-  const int bh = b * nh + h;
+  const int per_qb = batch * nh;
+  const int n_items = nkb * per_qb;  // items [0, per_qb) are the last query block: the most key blocks
+  const int P = gridDim.x, c = blockIdx.x;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kDqStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(acc, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_free[i], 4);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -462,62 +497,81 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     tma_prefetch_desc(&tm_out);
   }
   if (warp == 2) {
-    tmem_alloc(tmem_slot, 128);
+    tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;  // accumulators: columns [0,128) and [128,256)
 
   if (warp == 0) {
     if (lane == 0) {
-      const int kc = D + h * kHd;
-      int issued = 0;
-      for (int jj = 0; jj < nb; ++jj) {
-        const int st = jj % kDqStages;
-        const uint32_t ph = (jj / kDqStages) & 1;
-        if (!mbar_wait(&empty[st], ph ^ 1) || *abort_flag) {
-          set_error(err, kDevTimeoutProducer);
-          *abort_flag = 1;
-          break;
+      int g = 0, issued = 0;  // ring slots used so far / whose loads were issued
+      bool ok = true;
+      for (int t = 0; ok; ++t) {
+        const int item = dq_item(c, P, t);
+        if (item >= n_items) break;
+        const int qb = nkb - 1 - item / per_qb, rem = item % per_qb;
+        const int b = rem / nh, h = rem % nh, bh = b * nh + h;
+        const int kc = D + h * kHd, tok0 = b * S;
+        for (int jj = 0; jj <= qb; ++jj, ++g) {
+          const int st = g % kDqStages;
+          const uint32_t ph = (g / kDqStages) & 1;
+          if (!mbar_wait(&empty[st], ph ^ 1) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          uint8_t* s = smem + st * DqSmem::STAGE;
+          mbar_arrive_expect_tx(&full[st], DqSmem::STAGE);
+          // dS^T of sub-blocks 2 qb and 2 qb + 1 (consecutive 128-row tiles of the scratch)
+          tma_load_2d(s, &tm_ds2, &full[st], 0, ((bh * nkb + jj) * nsub + 2 * qb) * kKeys);
+          tma_load_2d(s + kKvTile, &tm_kv, &full[st], kc, tok0 + jj * kKeys);
+          tma_load_2d(s + kKvTile + kKvAtom, &tm_kv, &full[st], kc + 64, tok0 + jj * kKeys);
+          issued = g + 1;
         }
-        uint8_t* s = smem + st * DqSmem::STAGE;
-        mbar_arrive_expect_tx(&full[st], DqSmem::STAGE);
-        // dS^T of sub-blocks 2 qb and 2 qb + 1 (consecutive 128-row tiles of the scratch)
-        tma_load_2d(s, &tm_ds2, &full[st], 0, ((bh * nkb + jj) * nsub + 2 * qb) * kKeys);
-        tma_load_2d(s + kKvTile, &tm_kv, &full[st], kc, tok0 + jj * kKeys);
-        tma_load_2d(s + kKvTile + kKvAtom, &tm_kv, &full[st], kc + 64, tok0 + jj * kKeys);
-        issued = jj + 1;
       }
-      if (*abort_flag)
-        for (int jj = (issued > kDqStages ? issued - kDqStages : 0); jj < issued; ++jj)
-          mbar_wait(&full[jj % kDqStages], (jj / kDqStages) & 1);
+      if (!ok) {  // let copies still in flight land before the CTA exits
+        set_error(err, kDevTimeoutProducer);
+        *abort_flag = 1;
+        for (int x = (issued > kDqStages ? issued - kDqStages : 0); x < issued; ++x)
+          mbar_wait(&full[x % kDqStages], (x / kDqStages) & 1);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // dQ (128 queries x 128) += dS_j (queries contiguous) K_j (head dim contiguous); K = 128 keys
       constexpr uint32_t idesc = idesc_bf16_f32(kKeys, kHd, true, true);
       bool ok = true;
-      for (int jj = 0; jj < nb; ++jj) {
-        const int st = jj % kDqStages;
-        if (!mbar_wait(&full[st], (jj / kDqStages) & 1) || *abort_flag) {
+      int g = 0;
+      for (int t = 0; ok; ++t) {
+        const int item = dq_item(c, P, t);
+        if (item >= n_items) break;
+        const int nb = nkb - item / per_qb;  // key blocks 0 .. qb
+        const int ab = t & 1;
+        if (t >= 2 && (!mbar_wait(&acc_free[ab], ((t >> 1) - 1) & 1) || *abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t sa = smem_u32(smem + st * DqSmem::STAGE), sb = sa + kKvTile;
+        for (int jj = 0; jj < nb; ++jj, ++g) {
+          const int st = g % kDqStages;
+          if (!mbar_wait(&full[st], (g / kDqStages) & 1) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + st * DqSmem::STAGE), sb = sa + kKvTile;
 #pragma unroll
-        for (int kk = 0; kk < kKeys / 16; ++kk)
-          umma_bf16(tmem, smem_desc_sw128(sa + kk * 2048, kKvAtom, 1024), smem_desc_sw128(sb + kk * 2048, kKvAtom, 1024),
-                    idesc, (jj | kk) != 0 ? 1u : 0u);
-        umma_commit(&empty[st]);
+          for (int kk = 0; kk < kKeys / 16; ++kk)
+            umma_bf16(tmem + ab * kHd, smem_desc_sw128(sa + kk * 2048, kKvAtom, 1024),
+                      smem_desc_sw128(sb + kk * 2048, kKvAtom, 1024), idesc, (jj | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&acc_full[ab]);
       }
       if (!ok) {
         set_error(err, kDevTimeoutMma);
         *abort_flag = 1;
-      } else {
-        umma_commit(acc);
       }
       umma_commit(drain);
       mbar_wait(drain, 0);
@@ -525,56 +579,67 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   } else if (warp >= 4) {
     const int qw = warp & 3;
     const int r = qw * 32 + lane;  // query row within the block
-    const int qpos = qb * kKeys + r;
     const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
-    float rc[64], rs[64];  // RoPE tables of this query position, loaded while the MMAs run
+    uint8_t* stage_out = smem + DqSmem::OUT;
+    for (int t = 0;; ++t) {
+      const int item = dq_item(c, P, t);
+      if (item >= n_items) break;
+      const int qb = nkb - 1 - item / per_qb, rem = item % per_qb;
+      const int b = rem / nh, h = rem % nh;
+      const int qpos = qb * kKeys + r;
+      const int ab = t & 1;
+      float rc[64], rs[64];  // RoPE tables of this query position, loaded while the MMAs run
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      rc[i] = __ldg(cosb + static_cast<int64_t>(i) * S + qpos);
-      rs[i] = __ldg(sinb + static_cast<int64_t>(i) * S + qpos);
-    }
-    bool w = !*abort_flag && mbar_wait(acc, 0);
-    w = __all_sync(0xffffffffu, w);
-    if (!w) {
-      if (lane == 0) set_error(err, kDevTimeoutEpilogue);
-      *abort_flag = 1;
-    }
-    // every epilogue warp reaches the named barrier (a failed warp skips only its work)
-    if (w) {
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        float f[32];
-        tmem_ld32(tmem + lane_off + c * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float d0 = __uint_as_float(v[e]) * scale, d1 = __uint_as_float(v[e + 1]) * scale;
-          const float cc = rc[c * 16 + e / 2], ss = rs[c * 16 + e / 2];
-          f[e] = cc * d0 + ss * d1;
-          f[e + 1] = -ss * d0 + cc * d1;
-        }
-        // dQ tile in stage 0 (idle once the accumulator is complete): atom c / 2, chunks 4 (c % 2) ..
-        store_chunk32(smem + (c >> 1) * kKvAtom + r * 128, c & 1, r, f);
+      for (int i = 0; i < 64; ++i) {
+        rc[i] = __ldg(cosb + static_cast<int64_t>(i) * S + qpos);
+        rs[i] = __ldg(sinb + static_cast<int64_t>(i) * S + qpos);
       }
-      fence_proxy_async_smem();
+      bool w = !*abort_flag && mbar_wait(&acc_full[ab], (t >> 1) & 1);
+      w = __all_sync(0xffffffffu, w);
+      if (!w) {
+        if (lane == 0) set_error(err, kDevTimeoutEpilogue);
+        *abort_flag = 1;
+      }
+      if (threadIdx.x == 128) bulk_wait_read_all();  // the previous item's dQ has left the staging tile
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+      if (w) {
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t v[32];
+          float f[32];
+          tmem_ld32(tmem + ab * kHd + lane_off + cc * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float d0 = __uint_as_float(v[e]) * scale, d1 = __uint_as_float(v[e + 1]) * scale;
+            const float co = rc[cc * 16 + e / 2], si = rs[cc * 16 + e / 2];
+            f[e] = co * d0 + si * d1;
+            f[e + 1] = -si * d0 + co * d1;
+          }
+          store_chunk32(stage_out + (cc >> 1) * kKvAtom + r * 128, cc & 1, r, f);
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[ab]);  // this accumulator can take the item after next
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 128 && !*abort_flag) {
+        const int y = b * S + qb * kKeys;
+        tma_store_2d(&tm_out, stage_out, h * kHd, y);
+        tma_store_2d(&tm_out, stage_out + kKvAtom, h * kHd + 64, y);
+        bulk_commit();
+      }
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
-    if (threadIdx.x == 128 && !*abort_flag) {
-      const int y = tok0 + qb * kKeys;
-      tma_store_2d(&tm_out, smem, h * kHd, y);
-      tma_store_2d(&tm_out, smem + kKvAtom, h * kHd + 64, y);
-      bulk_commit();
-      bulk_wait_read_all();
-    }
+    if (threadIdx.x == 128) bulk_wait_read_all();
     tc_fence_before();
   }
 
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -612,8 +677,10 @@ int attn_backward_tc(const AttnArgs& a, cudaStream_t s) {
   attn_bwd_kv_tc_kernel<<<grid, kKvThreads, KvSmem::BYTES, s>>>(tm_kv, tm_do, tm_ds, tm_out, a.lse2, a.dvec, a.D,
                                                                a.S, a.heads, scale, scale_log2, a.rope_cos_b,
                                                                a.rope_sin_b, a.err);
-  attn_bwd_dq_tc_kernel<<<grid, kDqThreads, DqSmem::BYTES, s>>>(tm_kv, tm_ds2, tm_out, a.D, a.S, a.heads, scale,
-                                                               a.rope_cos_b, a.rope_sin_b, a.err);
+  const int dq_items = (a.S / kKeys) * a.batch * a.heads;
+  const int dq_grid = dq_items < num_sms() ? dq_items : num_sms();
+  attn_bwd_dq_tc_kernel<<<dq_grid, kDqThreads, DqSmem::BYTES, s>>>(tm_kv, tm_ds2, tm_out, a.D, a.S, a.heads, a.batch,
+                                                                   scale, a.rope_cos_b, a.rope_sin_b, a.err);
   return cudaGetLastError();
 }
 

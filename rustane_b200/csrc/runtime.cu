@@ -1184,6 +1184,30 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
 
 RT_API int rt_ctx_destroy(rt_ctx* c) {
   if (!c) return RT_ERR_ARG;
+  cudaSetDevice(c->device);
+  if (c->nccl && c->nccl->comm) {
+    // work still queued behind a collective whose peer has left would never finish:
+    // give it the context's timeout, then abort the communicator so the streams drain
+    rt::NcclApi* api = rt::nccl_api();
+    const auto t0 = std::chrono::steady_clock::now();
+    const int64_t limit_ms = std::max<int64_t>(c->timeout_ms, 1000);
+    auto busy = [&] {
+      for (cudaStream_t s : {c->stream, c->s_dw, c->s_comm})
+        if (s && cudaStreamQuery(s) == cudaErrorNotReady) return true;
+      return false;
+    };
+    while (busy()) {
+      const auto ms =
+          std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+      if (ms > limit_ms) {
+        if (api) api->commAbort(c->nccl->comm);
+        c->nccl->comm = nullptr;
+        c->nccl->aborted = true;
+        break;
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+  }
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->s_dw) cudaStreamSynchronize(c->s_dw);
   if (c->s_comm) cudaStreamSynchronize(c->s_comm);

@@ -8,6 +8,8 @@ It parses the loss0 column of the parameter-sweep tables
 init and tokens (i*31+7) % vocab, so they pin the oracle's embedding, final
 RMSNorm, tied logits and cross-entropy; every layer is an identity map at that
 init (wo = w2 = 0), which makes loss0 independent of the layer count.
+The sweep rows also carry the recorded loss after the 10-step protocol
+(`loss10`, bench_param_sweep.rs:85-101), which depends on the training math.
 """
 from __future__ import annotations
 
@@ -29,17 +31,21 @@ def parse(root: Path) -> list[dict]:
         try:
             name = cells[0].split(" ")[0]
             dim, hidden, heads, layers, seq = (int(cells[i]) for i in (2, 3, 4, 5, 6))
-            loss0 = float(cells[13])
+            loss0, loss10 = float(cells[13]), float(cells[14])
         except ValueError:
             continue
         rows.append(dict(name=name, dim=dim, hidden=hidden, heads=heads, nlayers=layers, seq=seq, loss0=loss0,
-                         decimals=3, source=f"results/2026-03-18_1830_param-sweep.md:{ln}"))
+                         loss10=loss10, decimals=3, source=f"results/2026-03-18_1830_param-sweep.md:{ln}"))
     readme = (root / "README.md").read_text().splitlines()
     for ln, line in enumerate(readme, start=1):
         m = re.search(r"Forward pass\.\.\. loss=(\d+\.\d{4})", line)
         if m:
             rows.append(dict(name="600m-A", dim=1536, hidden=4096, heads=12, nlayers=20, seq=512,
                              loss0=float(m.group(1)), decimals=4, source=f"README.md:{ln}"))
+        m = re.search(r"Training 10 steps\.\.\. (\d+\.\d{4}) → (\d+\.\d{4})", line)
+        if m:
+            rows.append(dict(name="600m-A", dim=1536, hidden=4096, heads=12, nlayers=20, seq=512,
+                             loss0=float(m.group(1)), loss10=float(m.group(2)), decimals=4, source=f"README.md:{ln}"))
         m = re.search(r"\(loss=(\d+\.\d{4})\)", line)
         if m and "ms" in line:
             rows.append(dict(name="7B", dim=4096, hidden=11008, heads=32, nlayers=32, seq=512,
