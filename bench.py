@@ -321,6 +321,7 @@ def main() -> None:
         dist.broadcast_object_list(uid, src=0)
         mode = _lib.RT_DIST_DATA_PARALLEL if train else _lib.RT_DIST_TENSOR_PARALLEL
         k.dist_init(world, rank, uid[0], mode, timeout_ms=120000)
+    nccl_ranks = k.dist_ranks()
     k.init_normal(seed=SEED_WEIGHTS, std=0.02)
 
     rng = np.random.default_rng(1000 + (rank if train else 0))  # TP ranks share the batch
@@ -434,6 +435,7 @@ def main() -> None:
                    "weights": ("N(0,0.02) seed 1234, fp32 master + AdamW state" if train
                                else "N(0,0.02) seed 1234, bf16"),
                    "tokens": "uniform ids, seed 1000+rank" if train else "uniform ids, seed 1000",
+                   "nccl_ranks": nccl_ranks,
                    "l2": "not flushed: every step streams > 10 GB of weights/grads/optimizer state (>> 126 MB L2)"},
         "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM (all projections, FFN, logits, data and weight grads)",
                      "achieved": gemm_tflops, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",

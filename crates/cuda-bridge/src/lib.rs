@@ -175,6 +175,7 @@ extern "C" {
     pub fn rt_nccl_unique_id(out128: *mut u8) -> c_int;
     pub fn rt_tp_shard(heads: c_int, hidden: c_int, world: c_int, rank: c_int, head0: *mut c_int, heads_loc: *mut c_int, hid0: *mut c_int, hid_loc: *mut c_int) -> c_int;
     pub fn rt_dist_init(ctx: *mut rt_ctx, world: c_int, rank: c_int, unique_id128: *const u8, mode: c_int, timeout_ms: c_int) -> c_int;
+    pub fn rt_dist_ranks(ctx: *const rt_ctx, nranks_out: *mut c_int) -> c_int;
     pub fn rt_grad_allreduce(ctx: *mut rt_ctx) -> c_int;
     pub fn rt_profile(ctx: *mut rt_ctx, enable: c_int) -> c_int;
     pub fn rt_get_timings(ctx: *mut rt_ctx, out: *mut rt_timings) -> c_int;

@@ -288,6 +288,10 @@ RT_API int rt_tp_shard(int heads, int hidden, int world, int rank, int* head0, i
  * call returns RT_ERR_STATE.  A failed join (RT_ERR_NCCL) leaves the context
  * unchanged. */
 RT_API int rt_dist_init(rt_ctx* ctx, int world, int rank, const uint8_t* unique_id128, int mode, int timeout_ms);
+/* Ranks of the context's NCCL communicator as NCCL itself reports them
+ * (ncclCommCount); 1 without a communicator.  No reference counterpart: the
+ * reference runs on one device. */
+RT_API int rt_dist_ranks(const rt_ctx* ctx, int* nranks_out);
 /* Sum the gradients over the data-parallel ranks (one in-place all-reduce). */
 RT_API int rt_grad_allreduce(rt_ctx* ctx);
 

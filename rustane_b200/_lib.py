@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
     "rt_last_h2d_bytes": (c_int, [c_void_p, ctypes.POINTER(c_int64)]),
     "rt_nccl_unique_id": (c_int, [c_uint8_p]),
     "rt_dist_init": (c_int, [c_void_p, c_int, c_int, c_uint8_p, c_int, c_int]),
+    "rt_dist_ranks": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "rt_tp_shard": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
                             ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "rt_grad_allreduce": (c_int, [c_void_p]),

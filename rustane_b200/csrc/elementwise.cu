@@ -455,6 +455,66 @@ __global__ void __launch_bounds__(kCeThreads)
   }
 }
 
+// Forward and backward of the train step in one read of the logits: the row is
+// held in registers (kCeVec float4 per thread), so loss, lse and the bf16 dlogits
+// come out of the same pass (cross_entropy.rs:58-96 forward and backward).
+__global__ void __launch_bounds__(kCeThreads)
+    ce_fused_kernel(const float* __restrict__ logits, const uint32_t* __restrict__ tgt, float* __restrict__ row_loss,
+                    float* __restrict__ row_lse, __nv_bfloat16* __restrict__ dl, int V, float softcap, float scale) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const float4* lr = reinterpret_cast<const float4*>(logits + static_cast<int64_t>(m) * V);
+  uint2* o = reinterpret_cast<uint2*>(dl + static_cast<int64_t>(m) * V);
+  const int V4 = V >> 2;
+  const int t = static_cast<int>(tgt[m]);
+  float4 z[kCeVec];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kCeVec; ++j) {
+    const int c = threadIdx.x + j * kCeThreads;
+    if (c < V4) {
+      float4 v = __ldcs(lr + c);  // read once: keep it out of L2's way
+      v.x = capz(v.x, softcap);
+      v.y = capz(v.y, softcap);
+      v.z = capz(v.z, softcap);
+      v.w = capz(v.w, softcap);
+      z[j] = v;
+      mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+  }
+  mx = block_max(mx, red);
+  float se = 0.f;
+#pragma unroll
+  for (int j = 0; j < kCeVec; ++j) {
+    const int c = threadIdx.x + j * kCeThreads;
+    if (c < V4) se += __expf(z[j].x - mx) + __expf(z[j].y - mx) + __expf(z[j].z - mx) + __expf(z[j].w - mx);
+  }
+  se = block_sum(se, red);
+  const float lse = mx + logf(se);
+  const float inv_sc = softcap > 0.f ? 1.0f / softcap : 0.f;
+#pragma unroll
+  for (int j = 0; j < kCeVec; ++j) {
+    const int c = threadIdx.x + j * kCeThreads;
+    if (c < V4) {
+      const float zz[4] = {z[j].x, z[j].y, z[j].z, z[j].w};
+      float d[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float p = __expf(zz[e] - lse);
+        if (4 * c + e == t) {  // the target column: one thread of the row
+          p -= 1.f;
+          row_loss[m] = lse - zz[e];
+        }
+        const float th = zz[e] * inv_sc;                      // tanh(l / softcap) when capped
+        const float dz = softcap > 0.f ? 1.f - th * th : 1.f;  // full_model.rs:267-273
+        d[e] = p * scale * dz;
+      }
+      o[c] = make_uint2(pack_bf16x2(d[0], d[1]), pack_bf16x2(d[2], d[3]));
+    }
+  }
+  if (threadIdx.x == 0) row_lse[m] = lse;
+}
+
 __global__ void mean_reduce_kernel(const float* __restrict__ x, int n, float* __restrict__ out) {
   __shared__ double red[32];
   double s = 0.0;
@@ -483,11 +543,25 @@ __global__ void __launch_bounds__(kNormThreads) sumsq_partial_kernel(const float
   const int64_t n4 = n >> 2;
   const int64_t per = (n4 + gridDim.x - 1) / gridDim.x;
   const int64_t b = per * blockIdx.x, e = min(n4, b + per);
-  float s = 0.f;
-  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
-    const float4 v = reinterpret_cast<const float4*>(x)[i];
-    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  // eight independent 16-byte loads in flight per thread; fixed order, so the result is deterministic
+  constexpr int U = 8;
+  float acc[U] = {};
+  const int64_t step = static_cast<int64_t>(blockDim.x) * U;
+  int64_t i0 = b + threadIdx.x;
+  for (; i0 + (U - 1) * blockDim.x < e; i0 += step) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = __ldcs(reinterpret_cast<const float4*>(x) + i0 + u * blockDim.x);
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
   }
+  for (int64_t i = i0; i < e; i += blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    acc[0] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < U; ++u) s += acc[u];
   if (blockIdx.x == gridDim.x - 1)  // tail elements not covered by float4s
     for (int64_t i = (n4 << 2) + threadIdx.x; i < n; i += blockDim.x) s += x[i] * x[i];
   double d = s;
@@ -771,6 +845,12 @@ int ce_backward(const float* logits, const float* row_lse, const uint32_t* tgt, 
                 float softcap, float scale, cudaStream_t s) {
   if (V % 4) return -1;
   ce_backward_kernel<<<M, kCeThreads, 0, s>>>(logits, row_lse, tgt, dl, V, softcap, scale);
+  return cudaGetLastError();
+}
+int ce_fused(const float* logits, const uint32_t* tgt, float* row_loss, float* row_lse, __nv_bfloat16* dl, int M,
+             int V, float softcap, float scale, cudaStream_t s) {
+  if (V % 4 != 0 || V > 4 * kCeVec * kCeThreads) return -1;
+  ce_fused_kernel<<<M, kCeThreads, 0, s>>>(logits, tgt, row_loss, row_lse, dl, V, softcap, scale);
   return cudaGetLastError();
 }
 int mean_reduce(const float* row_loss, int M, float* out, cudaStream_t s) {

@@ -36,6 +36,10 @@ int ce_forward(const float* logits, const uint32_t* tgt, float* row_loss, float*
 // dl[m, v] = bf16(scale * (softmax(z)[v] - [v == t]) * (softcap ? 1 - tanh^2 : 1))
 int ce_backward(const float* logits, const float* row_lse, const uint32_t* tgt, __nv_bfloat16* dl, int M, int V,
                 float softcap, float scale, cudaStream_t s);
+// ce_forward and ce_backward in one read of the logits (the train step, where the
+// backward always follows): row_loss, row_lse and dl as the two kernels write them.
+int ce_fused(const float* logits, const uint32_t* tgt, float* row_loss, float* row_lse, __nv_bfloat16* dl, int M,
+             int V, float softcap, float scale, cudaStream_t s);
 // out[0] = sum(row_loss) / M (fixed-order tree, one block)
 int mean_reduce(const float* row_loss, int M, float* out, cudaStream_t s);
 

@@ -86,8 +86,10 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
   tn = r / gm;
 }
 
+// sigmoid by the SFU exponential and the fast (approximate, ~2 ulp) division: the
+// epilogue's results are rounded to bf16, so the IEEE division's extra work buys nothing
 __device__ __forceinline__ float silu_sigmoid(float x, float& sig) {
-  sig = 1.f / (1.f + __expf(-x));
+  sig = __fdividef(1.f, 1.f + __expf(-x));
   return x * sig;
 }
 

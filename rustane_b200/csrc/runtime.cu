@@ -57,6 +57,7 @@ struct NcclApi {
   decltype(&ncclGroupStart) groupStart = nullptr;
   decltype(&ncclGroupEnd) groupEnd = nullptr;
   decltype(&ncclCommGetAsyncError) getAsyncError = nullptr;
+  decltype(&ncclCommCount) commCount = nullptr;
   decltype(&ncclCommAbort) commAbort = nullptr;
   decltype(&ncclCommDestroy) commDestroy = nullptr;
   decltype(&ncclGetErrorString) errorString = nullptr;
@@ -89,6 +90,7 @@ static NcclApi* nccl_api() {
   RT_SYM(groupStart, "ncclGroupStart");
   RT_SYM(groupEnd, "ncclGroupEnd");
   RT_SYM(getAsyncError, "ncclCommGetAsyncError");
+  RT_SYM(commCount, "ncclCommCount");
   RT_SYM(commAbort, "ncclCommAbort");
   RT_SYM(commDestroy, "ncclCommDestroy");
   RT_SYM(errorString, "ncclGetErrorString");
@@ -622,7 +624,15 @@ int forward_impl(rt_ctx* c, int batch, float softcap) {
     g.epi = rt::kEpiF32; g.out = c->logits; g.ldo = V;
     if ((rc = gemm(c, g, "logits"))) return rc;
   }
-  RT_OTHER(1, rt::ce_forward(c->logits, c->cur->targets, c->row_loss, c->row_lse, M, V, softcap, c->stream), "ce fwd");
+  c->dl_ready = c->fuse_ce && !forward_only(c);
+  c->fuse_ce = false;
+  if (c->dl_ready)  // train step: loss and dlogits (full_model.rs:265-276) in one read of the logits
+    RT_OTHER(1, rt::ce_fused(c->logits, c->cur->targets, c->row_loss, c->row_lse, c->dl, M, V, softcap,
+                             c->fuse_ce_scale, c->stream),
+             "ce fwd+bwd");
+  else
+    RT_OTHER(1, rt::ce_forward(c->logits, c->cur->targets, c->row_loss, c->row_lse, M, V, softcap, c->stream),
+             "ce fwd");
   RT_OTHER(1, rt::mean_reduce(c->row_loss, M, c->d_loss, c->stream), "loss mean");
   if (pend) c->gather_pending = false;  // every segment has been waited for
   cudaEventRecord(c->ev[1], c->stream);
@@ -852,8 +862,10 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   int rc;
   cudaEventRecord(c->ev[2], ms);
   // dlogits * loss_scale (full_model.rs:265-276); CE mean over seq per sequence (cross_entropy.rs:92-95)
-  RT_OTHER(1, rt::ce_backward(c->logits, c->row_lse, c->cur->targets, c->dl, M, V, softcap, loss_scale / S, ms),
-           "ce bwd");
+  if (!c->dl_ready)
+    RT_OTHER(1, rt::ce_backward(c->logits, c->row_lse, c->cur->targets, c->dl, M, V, softcap, loss_scale / S, ms),
+             "ce bwd");
+  c->dl_ready = false;
   cudaEventRecord(c->ev_ce, ms);
   {  // dE += dl^T x_final   (full_model.rs:299-312) -- weight-gradient stream
     cudaStreamWaitEvent(ds, c->ev_ce, 0);
@@ -1656,6 +1668,8 @@ static int train_step_device(rt_ctx* c, const rt::TokenBatch& tb, uint32_t step,
   const int batch = tb.batch;
   c->cur = &tb;
   c->grads_zero_pending = true;  // grads.zero_out() (full_model.rs:675)
+  c->fuse_ce = true;  // the backward below always follows: dlogits come out of the forward's CE pass
+  c->fuse_ce_scale = tc->loss_scale / static_cast<float>(c->cfg.seq);
   if ((rc = forward_impl(c, batch, tc->softcap))) return rc;
   // data parallel: gradients are all-reduced bucket by bucket inside the backward
   c->overlap_allreduce = c->world > 1 && c->dist_mode == RT_DIST_DATA_PARALLEL;
@@ -1887,6 +1901,18 @@ RT_API int rt_dist_init(rt_ctx* c, int world, int rank, const uint8_t* unique_id
     c->zero = ok && c->d_sumsq;
     c->sharded_p = c->sharded_mv = c->sharded_g = false;
   }
+  return RT_OK;
+}
+
+RT_API int rt_dist_ranks(const rt_ctx* c, int* nranks_out) {
+  if (!c || !nranks_out) return RT_ERR_ARG;
+  *nranks_out = 1;
+  if (!c->nccl || !c->nccl->comm) return RT_OK;
+  rt::NcclApi* api = rt::nccl_api();
+  if (!api || !api->commCount) return RT_ERR_NCCL;
+  int n = 0;
+  if (api->commCount(c->nccl->comm, &n) != ncclSuccess) return RT_ERR_NCCL;
+  *nranks_out = n;
   return RT_OK;
 }
 

@@ -90,6 +90,11 @@ struct rt_ctx {
   float* d_loss = nullptr;  // [1]
   float* d_norm = nullptr;  // [1]
   bool norm_valid = false;  // d_norm holds the last computed gradient norm
+  // train step: the forward's cross-entropy also writes dlogits (scale fuse_ce_scale),
+  // so the backward that follows skips its own pass over the logits
+  bool fuse_ce = false;
+  float fuse_ce_scale = 0.f;
+  bool dl_ready = false;
   float* norm_partials = nullptr;
 
   // backward scratch

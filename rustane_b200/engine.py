@@ -258,6 +258,12 @@ class CompiledKernels:
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id) if unique_id is not None else None
         self._check(lib().rt_dist_init(self.handle, world, rank, buf, mode, timeout_ms))
 
+    def dist_ranks(self) -> int:
+        """Ranks of this context's NCCL communicator (ncclCommCount); 1 without one."""
+        n = ctypes.c_int()
+        self._check(lib().rt_dist_ranks(self.handle, ctypes.byref(n)))
+        return n.value
+
     def grad_allreduce(self) -> None:
         self._check(lib().rt_grad_allreduce(self.handle))
 
