@@ -917,16 +917,20 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     return gemm_launch_pair(g, -g.force_bn, stream);
   int bn = g.force_bn;
   if (bn != 128 && bn != 192 && bn != 256) {
-    // time ~ waves x tile width / efficiency: 128-wide tiles are closer to the
-    // shared-memory read limit (A is re-read per 128 columns), 256 is the best
-    // single-CTA width, and the CTA pair's 256 x 256 tile (half the B traffic
-    // per SM) measured 2-8% faster than it at equal wave counts.
+    // time ~ max(1, tiles / units) x tile width / efficiency.  Fractional waves, not
+    // whole ones: a partial last wave runs faster per tile (fewer SMs share HBM, L2
+    // and the power budget), which measured closer on every 600M shape.  The
+    // efficiencies are fitted to per-variant timings of the LM step's GEMM shapes
+    // (K = 1536 .. 8192): relative to the single-CTA 256-wide tile, single-CTA 192
+    // 1.075 and 128 0.80 (128-wide tiles sit at the shared-memory read limit: A is
+    // re-read per 128 columns), CTA pair 256 x 192 1.26, 256 x 256 1.19, 256 x 128 0.955
+    // (each SM of a pair reads only half of B).
+    auto waves = [](int t, int units) { return t > units ? double(t) / units : 1.0; };
     double best = 1e30;
     for (int cand : {256, 192, 128}) {
       if (swiglu && (cand == 192 || g.N % (cand / 2) != 0)) continue;
-      const double eff = cand == 256 ? 1.0 : (cand == 192 ? 0.95 : 0.82);
-      const int t = tiles_for(cand);
-      const double cost = double((t + sms - 1) / sms) * cand / eff;
+      const double eff = cand == 256 ? 1.0 : (cand == 192 ? 1.075 : 0.80);
+      const double cost = waves(tiles_for(cand), sms) * cand / eff;
       if (cost < best * 0.999) {
         best = cost;
         bn = cand;
@@ -935,10 +939,12 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     if (!g.shared_sms && (!swiglu || g.N % 128 == 0)) {
       const int pairs = sms / 2;
       int pbn = 0;
-      for (int cand : {256, 192}) {
+      for (int cand : {192, 256, 128}) {
         if (cand == 192 && (g.b_mn || swiglu)) continue;
+        if (swiglu && g.N % (cand / 2) != 0) continue;
         const int t2 = ((g.M + 255) / 256) * (swiglu ? g.N / (cand / 2) : (g.N + cand - 1) / cand);
-        const double cost2 = double((t2 + pairs - 1) / pairs) * cand / (cand == 256 ? 1.12 : 1.07);
+        const double eff2 = cand == 192 ? 1.26 : (cand == 256 ? 1.19 : 0.955);
+        const double cost2 = waves(t2, pairs) * cand / eff2;
         if (cost2 < best * 0.999) {
           best = cost2;
           pbn = cand;

@@ -45,9 +45,10 @@ struct GemmArgs {
   int n_half = 0;  // kEpiSwiglu / kEpiSwigluBwd: column offset of the h3 / dh3 half
   int* err = nullptr;
   int force_bn = 0;  // 0: choose from the wave count; 128/192/256 force a 1-CTA tile width, -256/-192/-128 the CTA-pair kernel
-  // Another GEMM may run on the SMs at the same time (a second stream): choose
-  // among the single-CTA kernels only.  Persistent CTA-pair grids lose more to
-  // SMs held by the other kernel (measured in the overlapped backward).
+  // Restrict the choice to the single-CTA kernels.  The LM step does not set it:
+  // with the fitted tile cost model, CTA-pair grids also win in the overlapped
+  // backward, where another stream's GEMMs share the SMs (600M step 196.5k ->
+  // 201k tok/s, same-box A/B).
   bool shared_sms = false;
 };
 

@@ -755,7 +755,6 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = W + o.w2; g.ldb = H; g.b_mn = true;
     g.M = M; g.N = H; g.K = D;
     g.epi = rt::kEpiSwigluBwd; g.aux = A.h13; g.ld_aux = 2 * H; g.out = c->dh13[p]; g.ldo = 2 * H; g.n_half = H;
-    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
     if ((rc = gemm(c, g, "dgate"))) return rc;
   }
   cudaEventRecord(c->ev_dgate[l], ms);
@@ -782,7 +781,6 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = W + o.w13; g.ldb = 2 * H; g.b_mn = false;
     g.M = M; g.N = D; g.K = 2 * H;
     g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
-    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
     if ((rc = gemm(c, g, "dx_ffn"))) return rc;
   }
   // RMSNorm2 backward + dy (layer.rs:1702-1706); dx2s = alpha * dx2
@@ -806,7 +804,6 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = W + o.wo; g.ldb = D; g.b_mn = false;
     g.M = M; g.N = cfg.q_dim; g.K = D;
     g.epi = rt::kEpiBf16; g.out = c->da; g.ldo = cfg.q_dim;
-    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
     if ((rc = gemm(c, g, "da"))) return rc;
   }
   {  // sdpaBwd1 + sdpaBwd2 + RoPE backward (layer.rs:1736-1798)
@@ -835,7 +832,6 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = W + o.wqkv; g.ldb = 3 * D; g.b_mn = false;
     g.M = M; g.N = D; g.K = 3 * D;
     g.epi = rt::kEpiF32; g.out = c->dx_tmp; g.ldo = D;
-    g.shared_sms = true;  // runs beside the weight-gradient GEMMs of the second stream
     if ((rc = gemm(c, g, "dx_attn"))) return rc;
   }
   // RMSNorm1 backward + dx2 (layer.rs:1853-1857); alpha * dx for the layer below, into the
