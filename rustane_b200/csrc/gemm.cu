@@ -917,19 +917,25 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     return gemm_launch_pair(g, -g.force_bn, stream);
   int bn = g.force_bn;
   if (bn != 128 && bn != 192 && bn != 256) {
-    // time ~ max(1, tiles / units) x tile width / efficiency.  Fractional waves, not
-    // whole ones: a partial last wave runs faster per tile (fewer SMs share HBM, L2
-    // and the power budget), which measured closer on every 600M shape.  The
-    // efficiencies are fitted to per-variant timings of the LM step's GEMM shapes
-    // (K = 1536 .. 8192): relative to the single-CTA 256-wide tile, single-CTA 192
-    // 1.075 and 128 0.80 (128-wide tiles sit at the shared-memory read limit: A is
-    // re-read per 128 columns), CTA pair 256 x 192 1.26, 256 x 256 1.19, 256 x 128 0.955
-    // (each SM of a pair reads only half of B).
-    auto waves = [](int t, int units) { return t > units ? double(t) / units : 1.0; };
+    // time ~ waves x tile width / efficiency, where a partial last wave costs
+    // 0.6 + 0.4 x its fill of a full one (its tiles run faster: fewer SMs share HBM,
+    // L2 and the power budget).  The 0.6 and the efficiencies are a least-squares fit
+    // (4% rms) to every variant timed on every 600M GEMM shape (K = 1536 .. 8192):
+    // relative to the single-CTA 256-wide tile, single-CTA 192 0.885 and 128 0.669
+    // (narrow tiles re-read A per tile and sit at the shared-memory read limit), CTA
+    // pair 256 x 256 1.137, 256 x 192 1.007, 256 x 128 0.777 (each SM of a pair reads
+    // only half of B).  The fit picks the fastest measured variant on 10 of the 11
+    // shapes (the 11th within 1.5%) and keeps pair 256 x 256 on the 7B / 30B shapes.
+    auto waves = [](int t, int units) {
+      if (t <= units) return 1.0;
+      const int full = t / units;
+      const double frac = double(t) / units - full;
+      return full + (frac > 0 ? 0.6 + 0.4 * frac : 0.0);
+    };
     double best = 1e30;
     for (int cand : {256, 192, 128}) {
       if (swiglu && (cand == 192 || g.N % (cand / 2) != 0)) continue;
-      const double eff = cand == 256 ? 1.0 : (cand == 192 ? 1.075 : 0.80);
+      const double eff = cand == 256 ? 1.0 : (cand == 192 ? 0.885 : 0.669);
       const double cost = waves(tiles_for(cand), sms) * cand / eff;
       if (cost < best * 0.999) {
         best = cost;
@@ -943,7 +949,7 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
         if (cand == 192 && (g.b_mn || swiglu)) continue;
         if (swiglu && g.N % (cand / 2) != 0) continue;
         const int t2 = ((g.M + 255) / 256) * (swiglu ? g.N / (cand / 2) : (g.N + cand - 1) / cand);
-        const double eff2 = cand == 192 ? 1.26 : (cand == 256 ? 1.19 : 0.955);
+        const double eff2 = cand == 192 ? 1.007 : (cand == 256 ? 1.137 : 0.777);
         const double cost2 = waves(t2, pairs) * cand / eff2;
         if (cost2 < best * 0.999) {
           best = cost2;
