@@ -348,33 +348,38 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
-// dgamma[d] = (accumulate ? dgamma[d] : 0) + sum_b part[b][d]: 32 columns per block,
-// warp w sums partials w, w+8, ... in order (loads unrolled by 4, all in flight),
-// then the 8 warp sums in order.
-__global__ void __launch_bounds__(256) dgamma_reduce_kernel(const float* __restrict__ part, int nblk,
-                                                            float* __restrict__ dgamma, int D, int accumulate) {
-  __shared__ float red[8][33];
+// dgamma[d] = (accumulate ? dgamma[d] : 0) + sum_b part[b][d]: 32 columns per block of
+// 32 warps; warp w sums partials w, w+32, ... in order (at most five rows at the 148-row
+// grid of the backward, all loads in flight), then the 32 warp sums in order.  Latency-
+// bound: with 8 warps per block the loop ran five dependent rounds of loads (7.5 us).
+constexpr int kDgWarps = 32;
+__global__ void __launch_bounds__(32 * kDgWarps) dgamma_reduce_kernel(const float* __restrict__ part, int nblk,
+                                                                     float* __restrict__ dgamma, int D,
+                                                                     int accumulate) {
+  __shared__ float red[kDgWarps][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int d = blockIdx.x * 32 + lane;
   float s = 0.f;
   if (d < D) {
     int b = warp;
-    for (; b + 24 < nblk; b += 32) {
-      const float a0 = part[static_cast<int64_t>(b) * D + d], a1 = part[static_cast<int64_t>(b + 8) * D + d];
-      const float a2 = part[static_cast<int64_t>(b + 16) * D + d], a3 = part[static_cast<int64_t>(b + 24) * D + d];
+    for (; b + 3 * kDgWarps < nblk; b += 4 * kDgWarps) {
+      const float a0 = part[static_cast<int64_t>(b) * D + d];
+      const float a1 = part[static_cast<int64_t>(b + kDgWarps) * D + d];
+      const float a2 = part[static_cast<int64_t>(b + 2 * kDgWarps) * D + d];
+      const float a3 = part[static_cast<int64_t>(b + 3 * kDgWarps) * D + d];
       s += a0;
       s += a1;
       s += a2;
       s += a3;
     }
-    for (; b < nblk; b += 8) s += part[static_cast<int64_t>(b) * D + d];
+    for (; b < nblk; b += kDgWarps) s += part[static_cast<int64_t>(b) * D + d];
   }
   red[warp][lane] = s;
   __syncthreads();
   if (warp == 0 && d < D) {
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) t += red[w][lane];
+    for (int w = 0; w < kDgWarps; ++w) t += red[w][lane];
     dgamma[d] = accumulate ? dgamma[d] + t : t;
   }
 }
@@ -643,6 +648,28 @@ __global__ void sumsq_final_kernel(const float* __restrict__ partials, int n, fl
   }
 }
 
+// out[0] = sum of n floats (fixed order: strided per thread in double, then a fixed
+// tree), out[1 .. nout) = 0: folds the per-warp sums of squares the weight-gradient
+// GEMMs wrote into a gradient segment's grad-norm partial slots.
+__global__ void __launch_bounds__(256) sumsq_fold_kernel(const float* __restrict__ in, int n,
+                                                         float* __restrict__ out, int nout) {
+  __shared__ double red[8];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += in[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w];
+    out[0] = static_cast<float>(t);
+  }
+  for (int i = 1 + threadIdx.x; i < nout; i += blockDim.x) out[i] = 0.f;
+}
+
 __global__ void sqrt_to_float_kernel(const double* __restrict__ sq, float* __restrict__ out) {
   out[0] = static_cast<float>(sqrt(sq[0]));
 }
@@ -878,7 +905,7 @@ int rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float
   return cudaGetLastError();
 }
 int dgamma_reduce(const float* part, int nblk, float* dgamma, int D, int accumulate, cudaStream_t s) {
-  dgamma_reduce_kernel<<<(D + 31) / 32, 256, 0, s>>>(part, nblk, dgamma, D, accumulate);
+  dgamma_reduce_kernel<<<(D + 31) / 32, 32 * kDgWarps, 0, s>>>(part, nblk, dgamma, D, accumulate);
   return cudaGetLastError();
 }
 int ce_forward(const float* logits, const uint32_t* tgt, float* row_loss, float* row_lse, int M, int V,
@@ -908,6 +935,10 @@ int sumsq_seg_blocks() { return kSegNormBlocks; }
 int sumsq_partials(const float* x, int64_t n, float* partials, cudaStream_t s) {
   if (reinterpret_cast<uintptr_t>(x) & 15) return -1;
   sumsq_partial_kernel<<<kSegNormBlocks, kNormThreads, 0, s>>>(x, n, partials);
+  return cudaGetLastError();
+}
+int sumsq_fold(const float* in, int n, float* out, int nout, cudaStream_t s) {
+  sumsq_fold_kernel<<<1, 256, 0, s>>>(in, n, out, nout);
   return cudaGetLastError();
 }
 int sumsq_finish(const float* partials, int n, float* out_norm, cudaStream_t s) {

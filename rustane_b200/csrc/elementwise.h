@@ -51,6 +51,8 @@ int sumsq_partials_count();
 // L2 norm.  The train step reduces each layer's gradients as soon as they are final.
 int sumsq_seg_blocks();
 int sumsq_partials(const float* x, int64_t n, float* partials, cudaStream_t s);
+// out[0] = sum of in[0 .. n) (fixed order), out[1 .. nout) = 0.
+int sumsq_fold(const float* in, int n, float* out, int nout, cudaStream_t s);
 int sumsq_finish(const float* partials, int n, float* out_norm, cudaStream_t s);
 // The same reduction without the square root, in double (for a cross-rank sum),
 // and the square root of that sum into a float.

@@ -70,6 +70,8 @@ struct KParams {
   const float* rope_cos;
   const float* rope_sin;
   int* err;
+  float* sumsq;  // kEpiF32Acc: per-warp sums of squares of the output (nullptr: none)
+  int sumsq_slots;
 };
 
 // Tile order: groups of `group` M-tiles; inside a group M runs fastest, then N.
@@ -183,7 +185,7 @@ __device__ __forceinline__ void load_aux(const KParams& p, int mbase, int n, int
 // accumulators of row mbase + crow(i), columns n + ccol .. n + ccol + 3.
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const KParams& p, int mbase, int n, int lane, float4 (&w)[8],
-                                               const AuxRegs& a) {
+                                               const AuxRegs& a, float& ss) {
   const int col = n + ccol(lane);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -210,6 +212,7 @@ __device__ __forceinline__ void epilogue_chunk(const KParams& p, int mbase, int 
         v.z = o.z + p.alpha * v.z;
         v.w = o.w + p.alpha * v.w;
       }
+      if constexpr (EPI == kEpiF32Acc) ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
       *reinterpret_cast<float4*>(static_cast<float*>(p.out) + mr * p.ldo + col) = v;
     } else if constexpr (EPI == kEpiRope) {
       // Interleaved-pair rotation per head of 128 (kernels/sdpa_fwd.rs:18-33, 100-128):
@@ -252,7 +255,7 @@ __device__ __forceinline__ void epilogue_chunk(const KParams& p, int mbase, int 
 // warp's shared-memory transpose buffer.
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, uint32_t wbuf, int lane, int mbase,
-                                              int tn, int c0, int c1, AuxRegs& pre) {
+                                              int tn, int c0, int c1, AuxRegs& pre, float& ss) {
   if constexpr (EPI == kEpiSwiglu) {
     // Columns [0, BN/2) hold h1 = x W1, [BN/2, BN) hold h3 = x W3 for the
     // same BN/2 hidden units (kernels/ffn_fused.rs:46-63 semantics).
@@ -293,10 +296,21 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, 
       if (c + 1 < c1) load_aux<EPI>(p, mbase, n + 32, lane, nxt);
       float4 w[8];
       tmem_chunk_coalesced(tbase + c * 32, wbuf, lane, w);
-      if (n < p.N) epilogue_chunk<EPI>(p, mbase, n, lane, w, cur);
+      if (n < p.N) epilogue_chunk<EPI>(p, mbase, n, lane, w, cur, ss);
       cur = nxt;
     }
   }
+}
+
+// The warp's sum of squares into its slot; the first warp also zeroes the slots of
+// CTAs the grid does not have, so all sumsq_slots floats add up to the squared norm.
+__device__ __forceinline__ void write_sumsq_slots(const KParams& p, float ss, int slot, int used, bool zero_rest,
+                                                  int lane) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) p.sumsq[slot] = ss;
+  if (zero_rest)
+    for (int i = used + lane; i < p.sumsq_slots; i += 32) p.sumsq[i] = 0.f;
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
@@ -456,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c0 = half * NCH / 2, c1 = (half + 1) * NCH / 2;
     const uint32_t wbuf = smem_u32(smem + C::EPI_OFF + (warp - 4) * kEpiBufBytes);
     int local = 0;
+    float ss = 0.f;  // kEpiF32Acc: this warp's sum of squares over its tiles
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (local >> 1) & 1;
@@ -479,10 +494,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE) + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(p, tbase, wbuf, lane, mbase, tn, c0, c1, pre);
+      epilogue_tile<BN, EPI>(p, tbase, wbuf, lane, mbase, tn, c0, c1, pre, ss);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+    if constexpr (EPI == kEpiF32Acc) {
+      if (p.sumsq) write_sumsq_slots(p, ss, static_cast<int>(blockIdx.x) * kEpiWarps + (warp - 4),
+                                     static_cast<int>(gridDim.x) * kEpiWarps, blockIdx.x == 0 && warp == 4, lane);
     }
   }
 
@@ -690,6 +709,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t wbuf = smem_u32(smem + C::EPI_OFF + (warp - 4) * kEpiBufBytes);
     const uint32_t tempty0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);  // the leader's barriers
     int local = 0;
+    float ss = 0.f;  // kEpiF32Acc: this warp's sum of squares over its tiles
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (local >> 1) & 1;
@@ -713,10 +733,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + static_cast<uint32_t>(acc * C::ACC_STRIDE) + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(p, tbase, wbuf, lane, mbase, tn, c0, c1, pre);
+      epilogue_tile<BN, EPI>(p, tbase, wbuf, lane, mbase, tn, c0, c1, pre, ss);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + 8 * acc);
+    }
+    if constexpr (EPI == kEpiF32Acc) {
+      if (p.sumsq)
+        write_sumsq_slots(p, ss, pair * 2 * kEpiWarps + static_cast<int>(rank) * kEpiWarps + (warp - 4),
+                          npairs * 2 * kEpiWarps, pair == 0 && rank == 0 && warp == 4, lane);
     }
   }
 
@@ -828,6 +853,8 @@ int g_num_sms = 0;
 
 }  // namespace
 
+int gemm_sumsq_slots() { return kEpiWarps * num_sms(); }
+
 int num_sms() {
   if (g_num_sms == 0) {
     int dev = 0;
@@ -866,6 +893,8 @@ int gemm_launch_pair(const GemmArgs& g, int bn, cudaStream_t stream) {
   kp.rope_cos = g.rope_cos;
   kp.rope_sin = g.rope_sin;
   kp.err = g.err;
+  kp.sumsq = g.sumsq;
+  kp.sumsq_slots = g.sumsq_slots;
 
   CUtensorMap ta, tb;
   bool ok;
@@ -905,6 +934,7 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   const bool swiglu = g.epi == kEpiSwiglu;
   if (swiglu && (!g.b_mn || g.n_half % 64 != 0 || g.N % 64 != 0)) return -1;
   if (g.epi == kEpiRope && (g.seq <= 0 || g.rope_cols % 128 != 0)) return -1;
+  if (g.sumsq && (g.epi != kEpiF32Acc || g.sumsq_slots < gemm_sumsq_slots())) return -1;
 
   const int sms = num_sms();
   auto tiles_for = [&](int bn) {
@@ -982,6 +1012,8 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   kp.rope_cos = g.rope_cos;
   kp.rope_sin = g.rope_sin;
   kp.err = g.err;
+  kp.sumsq = g.sumsq;
+  kp.sumsq_slots = g.sumsq_slots;
 
   CUtensorMap ta, tb;
   bool ok;

@@ -50,6 +50,12 @@ struct GemmArgs {
   // backward, where another stream's GEMMs share the SMs (600M step 196.5k ->
   // 201k tok/s, same-box A/B).
   bool shared_sms = false;
+  // kEpiF32Acc only: sum of squares of the written (final) values, one float per
+  // epilogue warp of every CTA (slot = CTA * 8 + warp; CTA pairs: pair * 16 + rank * 8
+  // + warp), the slots of CTAs the grid does not have set to zero, so the
+  // sumsq_slots floats always add up to the output's squared norm in a fixed order.
+  float* sumsq = nullptr;
+  int sumsq_slots = 0;  // at least gemm_sumsq_slots()
 };
 
 // Returns a cudaError_t-compatible code (0 = launched) or -1 on bad arguments.
@@ -59,5 +65,7 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream);
 bool make_tmap_bf16(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
                     uint32_t box_inner, uint32_t box_outer);
 int num_sms();
+// Floats a GemmArgs::sumsq buffer needs (8 per SM).
+int gemm_sumsq_slots();
 
 }  // namespace rt

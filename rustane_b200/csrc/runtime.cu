@@ -733,6 +733,16 @@ int zero_gather(rt_ctx* c, bool params, bool moments, bool grads) {
 // input and, for l > 0, dffn[(l - 1) & 1] = bf16(alpha * dy_next).  Weight
 // gradients go to the arena (beta = 0 overwrites) on the weight-gradient stream,
 // whose last GEMM records ev_dw_done[l].
+// Train step on one GPU: the weight-gradient GEMM k of layer l also writes its
+// per-warp sums of squares of the final gradient, which the grad norm folds in
+// instead of re-reading the layer's gradients.  (Data-parallel steps reduce the
+// gradients across ranks first, so their norm reads the reduced values.)
+void fold_sumsq(rt_ctx* c, rt::GemmArgs& g, int l, int k) {
+  if (!c->layer_sumsq || c->overlap_allreduce) return;
+  g.sumsq = c->gemm_sumsq + (int64_t(l) * 4 + k) * c->gemm_sumsq_slots;
+  g.sumsq_slots = c->gemm_sumsq_slots;
+}
+
 int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) {
   const auto& cfg = c->cfg;
   const int D = cfg.dim, H = cfg.hidden, S = cfg.seq, L = cfg.nlayers;
@@ -765,6 +775,7 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = A.gate; g.ldb = H; g.b_mn = true;
     g.M = D; g.N = H; g.K = M;
     g.epi = rt::kEpiF32Acc; g.out = Gr + o.w2; g.ldo = H; g.beta = beta;
+    fold_sumsq(c, g, l, 0);
     if ((rc = gemm(c, g, "dW2", ds))) return rc;
   }
   {  // dW1 | dW3 += x2norm^T (dh1 | dh3) (layer.rs:1692, 1787)
@@ -773,6 +784,7 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = c->dh13[p]; g.ldb = 2 * H; g.b_mn = true;
     g.M = D; g.N = 2 * H; g.K = M;
     g.epi = rt::kEpiF32Acc; g.out = Gr + o.w13; g.ldo = 2 * H; g.beta = beta;
+    fold_sumsq(c, g, l, 1);
     if ((rc = gemm(c, g, "dW13", ds))) return rc;
   }
   {  // ffnBwdW13t: dx_ffn = dh1 W1^T + dh3 W3^T (layer.rs:1671-1699)
@@ -796,6 +808,7 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = c->dx2s[p]; g.ldb = D; g.b_mn = true;
     g.M = cfg.q_dim; g.N = D; g.K = M;
     g.epi = rt::kEpiF32Acc; g.out = Gr + o.wo; g.ldo = D; g.beta = beta;
+    fold_sumsq(c, g, l, 2);
     if ((rc = gemm(c, g, "dWo", ds))) return rc;
   }
   {  // wotBwd: da = dx2s Wo^T (layer.rs:1709-1733)
@@ -823,6 +836,7 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.b = c->dqkv[p]; g.ldb = 3 * D; g.b_mn = true;
     g.M = D; g.N = 3 * D; g.K = M;
     g.epi = rt::kEpiF32Acc; g.out = Gr + o.wqkv; g.ldo = 3 * D; g.beta = beta;
+    fold_sumsq(c, g, l, 3);
     if ((rc = gemm(c, g, "dWqkv", ds))) return rc;
   }
   cudaEventRecord(c->ev_dw_done[l], ds);
@@ -903,7 +917,12 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
       rc = shard ? reduce_scatter_seg(c, 1 + l, c->s_comm) : allreduce_range(c, o.wqkv, o.w2 + int64_t(D) * H, c->s_comm);
       if (rc) return rc;
     }
-    if (seg_norm) {  // sharded: this rank's chunk only (the ranks' sums are added after the backward)
+    if (seg_norm && !c->overlap_allreduce) {  // the layer's dW GEMMs wrote their sums of squares
+      const int ns = 4 * c->gemm_sumsq_slots;
+      RT_OTHER_ON(c->s_comm, 1,
+                  rt::sumsq_fold(c->gemm_sumsq + int64_t(l) * ns, ns, c->norm_partials + (1 + l) * SB, SB, c->s_comm),
+                  "grad norm");
+    } else if (seg_norm) {  // sharded: this rank's chunk only (the ranks' sums are added after the backward)
       const int64_t b0 = shard ? seg_own(c, 1 + l) : o.wqkv;
       const int64_t n = shard ? seg_chunk(c, 1 + l) : o.w2 + int64_t(D) * H - o.wqkv;
       RT_OTHER_ON(c->s_comm, 1, rt::sumsq_partials(Gr + b0, n, c->norm_partials + (1 + l) * SB, c->s_comm),
@@ -1142,6 +1161,9 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
                   (void*)c->row_lse, (void*)c->d_loss, (void*)c->d_norm, (void*)c->norm_partials, (void*)c->dy_a})
     need(p);
   if (!fo) {
+    c->gemm_sumsq_slots = rt::gemm_sumsq_slots();
+    c->gemm_sumsq = dalloc<float>(c, int64_t(cfg.nlayers) * 4 * c->gemm_sumsq_slots);
+    need(c->gemm_sumsq);
     c->dl = dalloc<bf16>(c, M * V);
     c->dy_b = dalloc<float>(c, M * D);
     c->dx_tmp = dalloc<float>(c, M * D);

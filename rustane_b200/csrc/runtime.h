@@ -89,6 +89,10 @@ struct rt_ctx {
   float* row_lse = nullptr;
   float* d_loss = nullptr;  // [1]
   float* d_norm = nullptr;  // [1]
+  // per layer and weight-gradient GEMM (dW2, dW13, dWo, dWqkv): the GEMM epilogue's
+  // per-warp sums of squares of the final gradient (gemm_sumsq_slots floats each)
+  float* gemm_sumsq = nullptr;
+  int gemm_sumsq_slots = 0;
   bool norm_valid = false;  // d_norm holds the last computed gradient norm
   // train step: the forward's cross-entropy also writes dlogits (scale fuse_ce_scale),
   // so the backward that follows skips its own pass over the logits
