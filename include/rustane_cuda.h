@@ -311,6 +311,12 @@ RT_API int rt_get_timings(rt_ctx* ctx, rt_timings* out);
 #define RT_EPI_ROPE 4
 #define RT_EPI_SWIGLU 5
 #define RT_EPI_SWIGLU_BWD 6
+/* out = bf16(C) and out2 (fp32) [M/seq][N/128][seq] = per 128-column head, the
+ * sum of bf16(C) * aux (bf16 [M][ld_aux]) over the head's columns: the rowsum
+ * dO . O of the attention backward (sdpaBwd1, kernels/sdpa_bwd.rs:44-100) from
+ * the GEMM that produces dO.  K-major A and B, N % 128 == 0, M % seq == 0;
+ * 256-wide tiles (force_bn 0, 256 or -256). */
+#define RT_EPI_BF16_ROWDOT 7
 
 /* tcgen05 GEMM C[M,N] = sum_k A[m,k] B[n,k] (bf16 in, fp32 accumulate) with a
  * fused epilogue.  a_mn/b_mn select MN-major storage ([K][M] / [K][N]).

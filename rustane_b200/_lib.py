@@ -24,7 +24,7 @@ RT_ERR_ARG, RT_ERR_SHAPE, RT_ERR_CUDA, RT_ERR_OOM, RT_ERR_TOKEN, RT_ERR_DEVICE, 
 RT_CTX_TRAIN, RT_CTX_FORWARD_ONLY = 0, 1
 RT_DIST_DATA_PARALLEL, RT_DIST_TENSOR_PARALLEL = 0, 1
 
-EPI_BF16, EPI_F32, EPI_F32_ACC, EPI_RESIDUAL, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD = range(7)
+EPI_BF16, EPI_F32, EPI_F32_ACC, EPI_RESIDUAL, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_BF16_ROWDOT = range(8)
 
 
 class RtTrainConfig(ctypes.Structure):

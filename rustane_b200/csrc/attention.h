@@ -18,6 +18,9 @@ struct AttnArgs {
   const __nv_bfloat16* dout = nullptr;  // dO [M, lddo]
   int64_t lddo = 0;
   float* dvec = nullptr;  // [batch, heads, S] scratch: rowsum(dO * O)
+  // tcgen05 backward: dvec already holds rowsum(dO * O) (written by the epilogue of
+  // the GEMM that produced dO), so the rowsum pass is skipped.
+  bool dvec_ready = false;
   __nv_bfloat16* dqkv = nullptr;  // [M, lddq]: dQ | dK | dV (RoPE backward applied)
   int64_t lddq = 0;
   const float* rope_cos_b = nullptr;  // [hd/2][S]

@@ -669,8 +669,10 @@ int attn_backward_tc(const AttnArgs& a, cudaStream_t s) {
   const cudaError_t attr2 = smem_limit_once(reinterpret_cast<const void*>(attn_bwd_dq_tc_kernel), DqSmem::BYTES);
   if (attr1 != cudaSuccess) return attr1;
   if (attr2 != cudaSuccess) return attr2;
-  int rc = attn_bwd_rowsum(a, s);
-  if (rc) return rc;
+  if (!a.dvec_ready) {
+    const int rc = attn_bwd_rowsum(a, s);
+    if (rc) return rc;
+  }
   const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(a.heads, a.batch, a.S / kKeys);

@@ -167,6 +167,9 @@ __device__ __forceinline__ void load_aux(const KParams& p, int mbase, int n, int
       const uint2 h1 = *reinterpret_cast<const uint2*>(h13 + col);
       const uint2 h3 = *reinterpret_cast<const uint2*>(h13 + p.n_half + col);
       a.u[i] = make_uint4(h1.x, h1.y, h3.x, h3.y);
+    } else if constexpr (EPI == kEpiBf16RowDot) {
+      const uint2 o = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.aux) + mr * p.ld_aux + col);
+      a.u[i] = make_uint4(o.x, o.y, 0u, 0u);
     } else if constexpr (EPI == kEpiF32Acc) {
       if (p.beta) a.u[i] = *reinterpret_cast<const uint4*>(static_cast<const float*>(p.out) + mr * p.ldo + col);
     } else if constexpr (EPI == kEpiRope) {
@@ -285,6 +288,55 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, 
         *reinterpret_cast<uint2*>(h13 + p.n_half + col) = pack_bf16x4(u[i]);
         *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out2) + mr * p.ldo2 + col) =
             pack_bf16x4(make_float4(gt[0], gt[1], gt[2], gt[3]));
+      }
+    }
+  } else if constexpr (EPI == kEpiBf16RowDot) {
+    // The warp's chunks [c0, c1) are the 128 columns of one attention head
+    // (BN = 256: two heads per tile, one per epilogue half).  Each lane sums
+    // bf16(C) * O over its 4 columns of the 4 chunks for its 8 rows; the 8 lanes
+    // holding one row then combine in a fixed xor order.
+    static_assert(BN == 256, "row dot needs one whole head per epilogue warp");
+    float rd[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) rd[i] = 0.f;
+    AuxRegs cur = pre;
+#pragma unroll 1
+    for (int c = c0; c < c1; ++c) {
+      const int n = tn * BN + c * 32;
+      AuxRegs nxt;
+      if (c + 1 < c1) load_aux<EPI>(p, mbase, n + 32, lane, nxt);
+      float4 w[8];
+      tmem_chunk_coalesced(tbase + c * 32, wbuf, lane, w);
+      if (n < p.N) {
+        const int col = n + ccol(lane);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int m = mbase + crow(i, lane);
+          if (m >= p.M) continue;
+          const uint2 d2 = pack_bf16x4(w[i]);
+          *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + int64_t(m) * p.ldo + col) = d2;
+          const float4 d = unpack_bf16x4(d2.x, d2.y);
+          const float4 o = unpack_bf16x4(cur.u[i].x, cur.u[i].y);
+          rd[i] += (d.x * o.x + d.y * o.y) + (d.z * o.z + d.w * o.w);
+        }
+      }
+      cur = nxt;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      rd[i] += __shfl_xor_sync(0xffffffffu, rd[i], 1);
+      rd[i] += __shfl_xor_sync(0xffffffffu, rd[i], 2);
+      rd[i] += __shfl_xor_sync(0xffffffffu, rd[i], 4);
+    }
+    const int n0 = tn * BN + c0 * 32;
+    if (n0 < p.N && (lane & 7) == 0) {
+      const int head = n0 >> 7, heads = p.N >> 7;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = mbase + crow(i, lane);
+        if (m >= p.M) continue;
+        const int b = m / p.seq, pos = m - b * p.seq;
+        static_cast<float*>(p.out2)[(int64_t(b) * heads + head) * p.seq + pos] = rd[i];
       }
     }
   } else {
@@ -836,6 +888,10 @@ int dispatch2(const GemmArgs& g, const CUtensorMap& ta, const CUtensorMap& tb, c
   if (g.a_mn == AMN && g.b_mn == BMN && g.epi == EPI) return launch_inst2<BN, AMN, BMN, EPI>(ta, tb, kp, grid, s);
   RT_GEMM_COMBOS(RT_GEMM_CASE)
 #undef RT_GEMM_CASE
+  if constexpr (BN == 256) {
+    if (!g.a_mn && !g.b_mn && g.epi == kEpiBf16RowDot)
+      return launch_inst2<256, false, false, kEpiBf16RowDot>(ta, tb, kp, grid, s);
+  }
   return -1;
 }
 
@@ -846,6 +902,10 @@ int dispatch(const GemmArgs& g, const CUtensorMap& ta, const CUtensorMap& tb, co
   if (g.a_mn == AMN && g.b_mn == BMN && g.epi == EPI) return launch_inst<BN, AMN, BMN, EPI>(ta, tb, kp, grid, s);
   RT_GEMM_COMBOS(RT_GEMM_CASE)
 #undef RT_GEMM_CASE
+  if constexpr (BN == 256) {
+    if (!g.a_mn && !g.b_mn && g.epi == kEpiBf16RowDot)
+      return launch_inst<256, false, false, kEpiBf16RowDot>(ta, tb, kp, grid, s);
+  }
   return -1;
 }
 
@@ -872,6 +932,7 @@ int gemm_launch_pair(const GemmArgs& g, int bn, cudaStream_t stream) {
   const bool swiglu = g.epi == kEpiSwiglu;
   if (swiglu && g.N % (bn / 2) != 0) return -1;
   if (bn == 192 && (g.b_mn || swiglu)) return -1;
+  if (g.epi == kEpiBf16RowDot && bn != 256) return -1;
   KParams kp{};
   kp.M = g.M;
   kp.N = g.N;
@@ -935,6 +996,14 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (swiglu && (!g.b_mn || g.n_half % 64 != 0 || g.N % 64 != 0)) return -1;
   if (g.epi == kEpiRope && (g.seq <= 0 || g.rope_cols % 128 != 0)) return -1;
   if (g.sumsq && (g.epi != kEpiF32Acc || g.sumsq_slots < gemm_sumsq_slots())) return -1;
+  const bool rowdot = g.epi == kEpiBf16RowDot;
+  if (rowdot) {
+    // One head of 128 columns per epilogue warp: 256-wide tiles, K-major operands.
+    if (g.a_mn || g.b_mn || g.N % 128 != 0 || g.seq <= 0 || g.M % g.seq != 0 || !g.aux || !g.out2 ||
+        g.ld_aux % 4 != 0 || (reinterpret_cast<uintptr_t>(g.aux) & 7) || (reinterpret_cast<uintptr_t>(g.out2) & 3))
+      return -1;
+    if (g.force_bn != 0 && g.force_bn != 256 && g.force_bn != -256) return -1;
+  }
 
   const int sms = num_sms();
   auto tiles_for = [&](int bn) {
@@ -965,6 +1034,7 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     double best = 1e30;
     for (int cand : {256, 192, 128}) {
       if (swiglu && (cand == 192 || g.N % (cand / 2) != 0)) continue;
+      if (rowdot && cand != 256) continue;
       const double eff = cand == 256 ? 1.0 : (cand == 192 ? 0.885 : 0.669);
       const double cost = waves(tiles_for(cand), sms) * cand / eff;
       if (cost < best * 0.999) {
@@ -978,6 +1048,7 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
       for (int cand : {192, 256, 128}) {
         if (cand == 192 && (g.b_mn || swiglu)) continue;
         if (swiglu && g.N % (cand / 2) != 0) continue;
+        if (rowdot && cand != 256) continue;
         const int t2 = ((g.M + 255) / 256) * (swiglu ? g.N / (cand / 2) : (g.N + cand - 1) / cand);
         const double eff2 = cand == 192 ? 1.007 : (cand == 256 ? 1.137 : 0.777);
         const double cost2 = waves(t2, pairs) * cand / eff2;

@@ -17,6 +17,10 @@ enum GemmEpilogue : int {
   kEpiRope = 4,        // out(bf16) = C, interleaved-pair RoPE on columns < rope_cols
   kEpiSwiglu = 5,      // tile holds h1|h3 for BN/2 hidden units: out=h13(bf16), out2=gate(bf16)
   kEpiSwigluBwd = 6,   // C = dgate; aux = h13(bf16): out = dh13(bf16) (dh1 | dh3 halves)
+  // out(bf16) = C (= dO of attention); aux = O(bf16) [M][ld_aux]; out2(f32) =
+  // D[b][h][pos] = sum over head h's 128 columns of bf16(C) * O, m = b * seq + pos
+  // (the attention backward's rowsum).  256-wide tiles only, N % 128 == 0.
+  kEpiBf16RowDot = 7,
 };
 
 struct GemmArgs {

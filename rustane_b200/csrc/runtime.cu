@@ -816,7 +816,9 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     g.a = c->dx2s[p]; g.lda = D;
     g.b = W + o.wo; g.ldb = D; g.b_mn = false;
     g.M = M; g.N = cfg.q_dim; g.K = D;
-    g.epi = rt::kEpiBf16; g.out = c->da; g.ldo = cfg.q_dim;
+    g.out = c->da; g.ldo = cfg.q_dim;
+    // the epilogue also writes the attention backward's rowsum(dO * O) per head
+    g.epi = rt::kEpiBf16RowDot; g.aux = A.attn; g.ld_aux = cfg.q_dim; g.out2 = c->dvec; g.seq = S;
     if ((rc = gemm(c, g, "da"))) return rc;
   }
   {  // sdpaBwd1 + sdpaBwd2 + RoPE backward (layer.rs:1736-1798)
@@ -825,6 +827,7 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     a.qkv = A.qkv; a.ldq = 3 * D; a.out = A.attn; a.ldo = D; a.lse2 = A.lse2;
     a.dout = c->da; a.lddo = D; a.dvec = c->dvec; a.dqkv = c->dqkv[p]; a.lddq = 3 * D;
     a.rope_cos_b = c->rope_cos_b; a.rope_sin_b = c->rope_sin_b; a.err = c->d_err; a.ds_scratch = c->attn_ds;
+    a.dvec_ready = true;
     const double fl = 2.5 * 4.0 * batch * cfg.heads * double(S) * S / 2.0 * cfg.hd;
     RT_LAUNCH(launch(c, 1, fl, 3, [&] { return rt::attn_backward_tc(a, ms); }), "attention bwd");
   }

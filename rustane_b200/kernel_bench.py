@@ -16,7 +16,8 @@ import json
 from . import _lib
 
 EPIS = {"bf16": _lib.EPI_BF16, "f32": _lib.EPI_F32, "f32acc": _lib.EPI_F32_ACC, "residual": _lib.EPI_RESIDUAL,
-        "rope": _lib.EPI_ROPE, "swiglu": _lib.EPI_SWIGLU, "swiglu_bwd": _lib.EPI_SWIGLU_BWD}
+        "rope": _lib.EPI_ROPE, "swiglu": _lib.EPI_SWIGLU, "swiglu_bwd": _lib.EPI_SWIGLU_BWD,
+        "rowdot": _lib.EPI_BF16_ROWDOT}
 
 
 def _time(fn, iters, warmup=3):
@@ -45,11 +46,15 @@ def bench_gemm(args):
     out_cols = 2 * N if epi in (_lib.EPI_SWIGLU, _lib.EPI_SWIGLU_BWD) else N
     out = torch.zeros(M, out_cols, device="cuda", dtype=out_dtype)
     out2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16) if epi == _lib.EPI_SWIGLU else None
+    if epi == _lib.EPI_BF16_ROWDOT:
+        out2 = torch.empty(M // args.seq * (N // 128), args.seq, device="cuda")
     aux = None
     if epi == _lib.EPI_RESIDUAL:
         aux = torch.randn(M, N, device="cuda")
     elif epi == _lib.EPI_SWIGLU_BWD:
         aux = torch.randn(M, 2 * N, device="cuda").bfloat16()
+    elif epi == _lib.EPI_BF16_ROWDOT:
+        aux = torch.randn(M, N, device="cuda").bfloat16()
     rope = None
     if epi == _lib.EPI_ROPE:
         rope = (torch.rand(args.seq, 64, device="cuda"), torch.rand(args.seq, 64, device="cuda"))

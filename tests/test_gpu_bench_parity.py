@@ -15,9 +15,13 @@ loss within 2e-3 absolute; logits and every gradient tensor within 2e-2 of
 max|oracle| (normwise max relative error).  The AdamW update is checked in
 two parts: (1) the oracle's update_weights applied to the GPU's own gradients
 (same clip rule and learning-rate groups) must give the GPU's new weights
-within four fp32 ulps of each weight plus four ulps of its update (the device
-fuses w - lr * u into one multiply-add, so the update's own rounding shows in
-weights near zero, and it sums the norm in another order); (2) the loss of the next forward, GPU
+within four fp32 ulps of each weight plus eight ulps of its update.  The update
+term covers weights that the step carries to near zero (a weight of 1.47e-5
+moved by -1.50e-5 ends at -3.2e-7, so only the update's rounding shows): the
+device fuses the multiply-adds of m, v and w - lr * u, and its gradient norm
+(checked separately to 1e-5) sums in another order, which moves the clip scale
+by an ulp; together a few ulps of the update, measured up to 4.2 at the 600M
+width.  (2) the loss of the next forward, GPU
 weights after the step against oracle weights after the oracle's own step,
 within the loss tolerance.  A per-entry comparison of the two independent
 updates is not meaningful: the first AdamW step moves each entry by
@@ -139,16 +143,21 @@ def test_train_step_parity_bench_path(case):
     otc = po.default_train_config()
     gsc = np.float32(1.0) / (np.float32(batch) * np.float32(otc.loss_scale))
     raw = o.grad_norm(g_gpu)
+    assert abs(k.last_grad_norm() - raw) <= 1e-5 * raw, (k.last_grad_norm(), raw)
     combined = otc.grad_clip / raw if raw * gsc > otc.grad_clip else gsc
     w_chk = w0.copy()
     o.update_weights(w_chk, g_gpu, ModelOptState.zeros(cfg), 1, po.learning_rate(0, otc), otc, float(combined))
-    del g_gpu
     w1 = k.download_weights()
-    for (name, a), (_, b), (_, a0) in zip(w1.tensors(), w_chk.tensors(), w0.tensors()):
+    for (name, a), (_, b), (_, a0), (_, gg) in zip(w1.tensors(), w_chk.tensors(), w0.tensors(), g_gpu.tensors()):
         err = np.abs(a.astype(np.float64) - b)
-        bound = 4 * np.spacing(np.abs(b)).astype(np.float64) + 4 * np.spacing(np.abs(b - a0)).astype(np.float64)
-        assert np.all(err <= bound), (name, int(np.sum(err > bound)), float(err.max()))
-    del w_chk
+        bound = 4 * np.spacing(np.abs(b)).astype(np.float64) + 8 * np.spacing(np.abs(b - a0)).astype(np.float64)
+        if not np.all(err <= bound):
+            i = np.unravel_index(np.argmax(err - bound), err.shape)
+            raise AssertionError(
+                f"{name}: {int(np.sum(err > bound))} entries off; worst {i}: gpu {a[i]!r} oracle {b[i]!r} "
+                f"before {a0[i]!r} grad {gg[i]!r} scale {combined!r} gpu norm {k.last_grad_norm()!r} "
+                f"oracle norm {raw!r}")
+    del w_chk, g_gpu
 
     # (2) the next forward's loss after each side's own step
     loss2 = forward_staged(k)

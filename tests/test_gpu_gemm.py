@@ -219,3 +219,57 @@ def test_gemm_pair192_many_tiles(epi):
     base = acc.clone()
     gemm(At, True, Bt, False, M, N, K, _lib.EPI_F32_ACC, acc, beta=1, force_bn=PAIR192)
     assert _rel(acc, reft + base) < TOL
+
+
+def _rowdot_ref(out, O, seq):
+    M, N = out.shape
+    prod = (out.float() * O.float()).view(M // seq, seq, N // 128, 128).sum(-1)
+    return prod.permute(0, 2, 1).contiguous()  # [batch][head][pos]
+
+
+@pytest.mark.parametrize("bn", [0, 256, -256])
+@pytest.mark.parametrize("shape", [(576, 640, 384, 192), (4096, 1536, 1536, 512)])
+def test_gemm_bf16_rowdot(bn, shape):
+    # dO = dx2s Wo^T with the attention backward's rowsum(dO * O) per head in the
+    # epilogue: ragged M against 256-row tiles, an odd head count (the last tile's
+    # second half is outside N), and the 600M shape
+    M, N, K, seq = shape
+    A, B, ref = operands(M, N, K, False, False, seed=21)
+    g = torch.Generator(device="cuda").manual_seed(22)
+    O = torch.randn(M, N, generator=g, device="cuda").bfloat16()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    dvec = torch.full((M // seq, N // 128, seq), float("nan"), device="cuda")
+    gemm(A, False, B, False, M, N, K, _lib.EPI_BF16_ROWDOT, out, out2=dvec, aux=O, seq=seq, force_bn=bn)
+    assert _rel(out, ref) < 8e-3
+    if bn != 0:  # the same tile kernel without the row dot writes the same bits
+        plain = torch.empty_like(out)
+        gemm(A, False, B, False, M, N, K, _lib.EPI_BF16, plain, force_bn=bn)
+        assert torch.equal(plain, out)
+    want = _rowdot_ref(out, O, seq)
+    assert torch.isfinite(dvec).all()
+    assert ((dvec - want).norm() / want.norm()).item() < 1e-5
+
+
+def test_gemm_bf16_rowdot_rejects():
+    M, N, K, seq = 512, 384, 128, 256
+    A, B, _ = operands(M, N, K, False, False, seed=23)
+    O = torch.zeros(M, N, device="cuda").bfloat16()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    dvec = torch.empty(M // seq * (N // 128), seq, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    L = _lib.lib()
+
+    def call(n, bn, seq_, b_mn=0):
+        return L.rt_kernel_gemm(A.data_ptr(), A.stride(0), 0, B.data_ptr(), B.stride(0), b_mn, M, n, K,
+                                _lib.EPI_BF16_ROWDOT, out.data_ptr(), out.stride(0), dvec.data_ptr(), 0,
+                                O.data_ptr(), O.stride(0), 1.0, 0, None, None, seq_, 0, 0, bn, err.data_ptr(), st)
+
+    assert call(N, 128, seq) != 0     # tiles narrower than two heads
+    assert call(N, -128, seq) != 0
+    assert call(N - 32, 0, seq) != 0  # N not a whole number of heads
+    assert call(N, 0, 0) != 0         # no sequence length
+    assert call(N, 0, 384) != 0       # M not a whole number of sequences
+    assert call(N, 0, seq, b_mn=1) != 0
+    torch.cuda.synchronize()
+    assert err.item() == 0
