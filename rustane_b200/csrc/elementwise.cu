@@ -352,11 +352,15 @@ __global__ void __launch_bounds__(256, 1)
 // 32 warps; warp w sums partials w, w+32, ... in order (at most five rows at the 148-row
 // grid of the backward, all loads in flight), then the 32 warp sums in order.  Latency-
 // bound: with 8 warps per block the loop ran five dependent rounds of loads (7.5 us).
+// blockIdx.y selects one of several gammas: partials at part + y * part_stride, result
+// at dgamma + y * D (the gammas sit next to each other in the parameter arena).
 constexpr int kDgWarps = 32;
 __global__ void __launch_bounds__(32 * kDgWarps) dgamma_reduce_kernel(const float* __restrict__ part, int nblk,
                                                                      float* __restrict__ dgamma, int D,
-                                                                     int accumulate) {
+                                                                     int accumulate, int64_t part_stride) {
   __shared__ float red[kDgWarps][33];
+  part += blockIdx.y * part_stride;
+  dgamma += static_cast<int64_t>(blockIdx.y) * D;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int d = blockIdx.x * 32 + lane;
   float s = 0.f;
@@ -905,7 +909,14 @@ int rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float
   return cudaGetLastError();
 }
 int dgamma_reduce(const float* part, int nblk, float* dgamma, int D, int accumulate, cudaStream_t s) {
-  dgamma_reduce_kernel<<<(D + 31) / 32, 32 * kDgWarps, 0, s>>>(part, nblk, dgamma, D, accumulate);
+  dgamma_reduce_kernel<<<(D + 31) / 32, 32 * kDgWarps, 0, s>>>(part, nblk, dgamma, D, accumulate, 0);
+  return cudaGetLastError();
+}
+int dgamma_reduce_many(const float* part, int64_t part_stride, int nblk, float* dgamma, int D, int ngamma,
+                       int accumulate, cudaStream_t s) {
+  if (ngamma <= 0) return 0;
+  dgamma_reduce_kernel<<<dim3((D + 31) / 32, ngamma), 32 * kDgWarps, 0, s>>>(part, nblk, dgamma, D, accumulate,
+                                                                            part_stride);
   return cudaGetLastError();
 }
 int ce_forward(const float* logits, const uint32_t* tgt, float* row_loss, float* row_lse, int M, int V,

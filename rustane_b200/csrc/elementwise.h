@@ -28,6 +28,10 @@ int rmsnorm_bwd(const float* dy, const float* x, const float* gamma, const float
 int rmsnorm_bwd_blocks(int M);
 // dgamma[d] = (accumulate ? dgamma[d] : 0) + sum_b part[b][d]   (b ascending)
 int dgamma_reduce(const float* part, int nblk, float* dgamma, int D, int accumulate, cudaStream_t s);
+// The same for ngamma adjacent gammas in one launch: gamma g's partials at
+// part + g * part_stride, its result at dgamma + g * D (identical arithmetic).
+int dgamma_reduce_many(const float* part, int64_t part_stride, int nblk, float* dgamma, int D, int ngamma,
+                       int accumulate, cudaStream_t s);
 
 // Cross-entropy over rows of fp32 logits (optionally soft-capped):
 //   row_loss[m] = lse - z[t], row_lse[m] = lse, z = softcap > 0 ? softcap*tanh(l/softcap) : l.

@@ -751,7 +751,6 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
   const bf16* W = c->params_bf16;
   const float* P = c->params;
   float* Gr = c->grads;
-  const int nblk = rt::rmsnorm_bwd_blocks(M);
   cudaStream_t ms = c->stream, ds = c->s_dw;
   int rc;
   const rt::LayerActs& A = c->acts[l];
@@ -796,10 +795,9 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
     if ((rc = gemm(c, g, "dx_ffn"))) return rc;
   }
   // RMSNorm2 backward + dy (layer.rs:1702-1706); dx2s = alpha * dx2
-  RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s[p], alpha, c->dgamma_part,
-                              M, D, ms),
+  RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x2, P + o.gamma2, A.rms2, dy, c->dx2, c->dx2s[p], alpha,
+                              c->dgamma_part + (2 + 2 * l) * c->dgamma_stride, M, D, ms),
            "rmsnorm2 bwd");
-  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma2, D, beta, ms), "dgamma2");
   cudaEventRecord(c->ev_rms2[l], ms);
   cudaStreamWaitEvent(ds, c->ev_rms2[l], 0);
   {  // dWo += attn^T dx2s (layer.rs:1753)
@@ -855,9 +853,20 @@ int layer_backward(rt_ctx* c, int l, const float* dy, float* dy_next, int beta) 
   // other parity's dffn, last read by the weight GEMMs of layer l + 1
   if (l > 0 && l + 1 < L) cudaStreamWaitEvent(ms, c->ev_dw_done[l + 1], 0);
   RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, A.x, P + o.gamma1, A.rms1, c->dx2, dy_next,
-                              l > 0 ? c->dffn[(l - 1) & 1] : nullptr, alpha, c->dgamma_part, M, D, ms),
+                              l > 0 ? c->dffn[(l - 1) & 1] : nullptr, alpha,
+                              c->dgamma_part + (1 + 2 * l) * c->dgamma_stride, M, D, ms),
            "rmsnorm1 bwd");
-  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + o.gamma1, D, beta, ms), "dgamma1");
+  return RT_OK;
+}
+
+// dgamma of `ngamma` adjacent gammas from their partial slots, one launch
+// (slot 0 is the final norm's, at the arena's first gamma).
+int reduce_dgammas(rt_ctx* c, int slot0, int ngamma, int beta) {
+  const int M = c->cur_batch * c->cfg.seq, D = c->cfg.dim;
+  RT_OTHER(1, rt::dgamma_reduce_many(c->dgamma_part + slot0 * c->dgamma_stride, c->dgamma_stride,
+                                     rt::rmsnorm_bwd_blocks(M), c->grads + c->off_gamma_final + int64_t(slot0) * D, D,
+                                     ngamma, beta, c->stream),
+           "dgamma");
   return RT_OK;
 }
 
@@ -870,7 +879,6 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   const bf16* W = c->params_bf16;
   const float* P = c->params;
   float* Gr = c->grads;
-  const int nblk = rt::rmsnorm_bwd_blocks(M);
   cudaStream_t ms = c->stream, ds = c->s_dw;
   int rc;
   cudaEventRecord(c->ev[2], ms);
@@ -902,7 +910,6 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
   RT_OTHER(2, rt::rmsnorm_bwd(c->dx_tmp, c->x_out, P + c->off_gamma_final, c->rms_f, nullptr, c->dy_a,
                               c->dffn[(L - 1) & 1], alpha, c->dgamma_part, M, D, ms),
            "final rmsnorm bwd");
-  RT_OTHER(1, rt::dgamma_reduce(c->dgamma_part, nblk, Gr + c->off_gamma_final, D, beta, ms), "dgamma");
   float* dy = c->dy_a;
   float* dy_next = c->dy_b;
   // Gradient segments that are final go to the comm stream: all-reduced (data
@@ -933,6 +940,9 @@ int backward_impl(rt_ctx* c, float softcap, float loss_scale) {
     }
     std::swap(dy, dy_next);
   }
+  // dgamma of every RMSNorm from its partials in one launch (the gammas are the last
+  // gradient segment; nothing reads them during the backward)
+  if ((rc = reduce_dgammas(c, 0, 2 * L + 1, beta))) return rc;
   // embedding scatter-add (full_model.rs:330), after the dE GEMM
   cudaStreamWaitEvent(ms, c->ev_de, 0);
   RT_OTHER(1, rt::embed_scatter(dy, c->cur->perm, c->cur->seg_start, c->cur->seg_tok, c->cur->nseg, Gr, D, ms),
@@ -1184,7 +1194,8 @@ RT_API int rt_ctx_create(const rt_model_config* cfgp, int device, int max_batch,
     c->da = dalloc<bf16>(c, M * D);
     c->dvec = dalloc<float>(c, M * cfg.heads);
     c->attn_ds = dalloc<bf16>(c, static_cast<int64_t>(rt::attn_bwd_scratch_bytes(max_batch, S, cfg.heads) / 2));
-    c->dgamma_part = dalloc<float>(c, int64_t(rt::rmsnorm_bwd_blocks(static_cast<int>(M))) * D);
+    c->dgamma_stride = int64_t(rt::rmsnorm_bwd_blocks(static_cast<int>(M))) * D;
+    c->dgamma_part = dalloc<float>(c, (2 * int64_t(cfg.nlayers) + 1) * c->dgamma_stride);
     for (void* p : {(void*)c->dl, (void*)c->dy_b, (void*)c->dx_tmp, (void*)c->dx2, (void*)c->da, (void*)c->dvec,
                     (void*)c->attn_ds, (void*)c->dgamma_part})
       need(p);
@@ -1597,6 +1608,7 @@ int layer_backward_dev(rt_ctx* c, int l, int beta) {
   RT_OTHER(1, rt::cast_bf16_scaled(c->dy_a, c->dffn[l & 1], n, alpha_of(c->cfg), c->stream), "alpha * dy");
   int rc;
   if ((rc = layer_backward(c, l, c->dy_a, c->dy_b, beta))) return rc;
+  if ((rc = reduce_dgammas(c, 1 + 2 * l, 2, beta))) return rc;
   cudaStreamWaitEvent(c->stream, c->ev_dw_done[l], 0);
   return RT_OK;
 }

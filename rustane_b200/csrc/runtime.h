@@ -117,7 +117,11 @@ struct rt_ctx {
   rt::bf16* da = nullptr;  // [M, D]
   float* dvec = nullptr;     // [B, heads, S]
   rt::bf16* attn_ds = nullptr;  // dS^T tiles of the tcgen05 attention backward (B * heads * S * S)
+  // RMSNorm dgamma partials, one slot of dgamma_stride floats per gamma in arena order
+  // (slot 0 the final norm, 1 + 2l / 2 + 2l layer l's gamma1 / gamma2): the backward
+  // reduces all of them in one launch after its last layer.
   float* dgamma_part = nullptr;
+  int64_t dgamma_stride = 0;
 
   // tokens and the embedding-scatter segments: `io` is refilled by every call
   // that takes host tokens; `staged` slots hold batches uploaded ahead of time.
