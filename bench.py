@@ -24,7 +24,6 @@ import os
 import statistics
 import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -76,40 +75,60 @@ def workload_desc(cfg, name: str = "600m", batch: int = PER_GPU_BATCH) -> str:
 
 # --------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 50 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons every 50 ms, kept for the timed region only.
+
+    nvidia-smi is started before the warm-up (its start-up takes a good part of a
+    second on an 8-GPU box, longer than some timed regions); a reader thread stamps
+    each line on arrival and `summary()` keeps the lines stamped inside `window()`."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
-
-    def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
+        import threading
+        self.lines = []
+        self.t0 = self.t1 = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
-                 "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-i", str(gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, bufsize=1)
         except OSError:
             self.proc = None
-        return self
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        import atexit
+        atexit.register(self.close)  # no sampler outlives the run, whatever path it ends by
 
-    def __exit__(self, *exc):
-        if self.proc is not None:
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append((time.monotonic(), ln))
+
+    def window(self):
+        sampler = self
+
+        class _Window:
+            def __enter__(self):
+                sampler.t0 = time.monotonic()
+
+            def __exit__(self, *exc):
+                sampler.t1 = time.monotonic()
+        return _Window()
+
+    def close(self):
+        if self.proc is not None and self.proc.poll() is None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.thread.join(timeout=5)
 
     def summary(self) -> dict:
-        if not self.path or not os.path.exists(self.path):
+        self.close()
+        if self.proc is None or self.t0 is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        rows = [ln.split(",") for ln in open(self.path).read().splitlines() if ln.strip()]
-        os.unlink(self.path)
+        rows = [ln.split(",") for t, ln in self.lines if self.t0 <= t <= self.t1 and ln.strip()]
         sm, smax, power, reasons = [], None, [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for r in rows:
@@ -125,7 +144,8 @@ class ClockSampler:
                     reasons.add(name)
         under_load = [s for s, p in zip(sm, power) if p > 200.0] or sm
         return {"sm_mhz": statistics.median(under_load) if under_load else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(power) if power else None}
+                "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(power) if power else None,
+                "window_s": round(self.t1 - self.t0, 3)}
 
 
 # ------------------------------------------------------------ CPU oracle
@@ -225,6 +245,7 @@ def measure_workload(wl: str, B: int, K: int, W: int, rank: int, world: int, loc
                     k._check(L.rt_forward_staged(k.handle, step % 2, ctypes.c_float(0.0)))
                 step += 1
 
+        clocks = ClockSampler(local)
         steps(W)
         k._check(L.rt_sync(k.handle, None))
         sp = ctypes.c_void_p()
@@ -234,7 +255,7 @@ def measure_workload(wl: str, B: int, K: int, W: int, rank: int, world: int, loc
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
-        with ClockSampler(local) as clocks:
+        with clocks.window():
             ev0.record(stream)
             steps(K)
             k._check(L.rt_join(k.handle))
@@ -358,7 +379,8 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # -------- warm-up
+    # -------- warm-up (the clock sampler starts here, ready before the timed region)
+    clocks = ClockSampler(local)
     staged_steps(W)
     loss_w = ctypes.c_float()
     k._check(L.rt_sync(k.handle, ctypes.byref(loss_w)))
@@ -371,7 +393,7 @@ def main() -> None:
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    with clocks.window():
         ev0.record(stream)
         staged_steps(K)
         k._check(L.rt_join(k.handle))  # the last step's weight all-gathers (sharded data parallel) count too
