@@ -169,6 +169,22 @@ def test_published_init_loss_600m_full_depth():
     assert abs(loss - 9.0108) < LOSS_TOL
 
 
+@pytest.mark.parametrize("forward_only", [False, True], ids=["train-ctx", "forward-only-ctx"])
+def test_published_init_loss_7b_width(forward_only):
+    """7B forward, the reference init and tokens: 9.3228 (README.md:70).  Wo = W2 = 0 make
+    every layer an identity map at this init, so one layer at the 7B width gives the
+    32-layer loss; the forward-only context is the one the 7B bench line runs (bf16 weights)."""
+    cfg = ModelConfig.custom(4096, 11008, 32, 1)
+    w = full_model.random_weights(cfg)
+    tok, tgt = po.pattern_tokens(cfg)
+    k = CompiledKernels.compile(cfg, max_batch=1, forward_only=forward_only)
+    try:
+        loss = full_model.forward(cfg, k, w, tok, tgt)
+    finally:
+        k.close()
+    assert abs(loss - 9.3228) < LOSS_TOL, loss
+
+
 def test_exact_zero_grads_at_reference_init():
     """phase4_pretraining_checks.rs:30-76 on the GPU path (gpt_karpathy)."""
     cfg = ModelConfig.gpt_karpathy()
