@@ -51,6 +51,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 1 / x by the SFU's approximate instruction (PTX rcp.approx.ftz.f32: about 1 ulp,
+// 1 / inf = 0, denormal results flushed); used where the result is rounded to bf16.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes of work).
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;

@@ -232,22 +232,34 @@ __device__ __forceinline__ void epilogue_chunk(const KParams& p, int mbase, int 
       *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + mr * p.ldo + col) = pack_bf16x4(v);
     } else if constexpr (EPI == kEpiSwigluBwd) {
       // C = dgate = dffn * W2 (layer.rs:1627-1641); SiLU-gate backward
-      // (layer.rs:1660-1666): dh3 = dg * silu(h1); dh1 = dg * h3 * sig * (1 + h1 (1 - sig)).
+      // (layer.rs:1660-1666): dh3 = dg * silu(h1); dh1 = dg * h3 * sig * (1 + h1 (1 - sig)),
+      // sig = 1 / (1 + 2^(-h1 log2 e)) on the SFU, the rest in fp32 pairs (one instruction
+      // per two elements): the epilogue, not the MMAs, bounds this GEMM.
       const float4 h1 = unpack_bf16x4(a.u[i].x, a.u[i].y);
       const float4 h3 = unpack_bf16x4(a.u[i].z, a.u[i].w);
-      const float hv1[4] = {h1.x, h1.y, h1.z, h1.w}, hv3[4] = {h3.x, h3.y, h3.z, h3.w};
-      const float dg[4] = {v.x, v.y, v.z, v.w};
-      float d1[4], d3[4];
+      const uint64_t one2 = f2_pack(1.f, 1.f);
+      const uint64_t nl2 = f2_pack(-1.4426950408889634f, -1.4426950408889634f);
+      uint32_t o1[2], o3[2];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float sig;
-        const float sl = silu_sigmoid(hv1[e], sig);
-        d3[e] = dg[e] * sl;
-        d1[e] = dg[e] * hv3[e] * (sig * (1.f + hv1[e] * (1.f - sig)));
+      for (int e = 0; e < 2; ++e) {
+        const uint64_t x2 = e ? f2_pack(h1.z, h1.w) : f2_pack(h1.x, h1.y);
+        const uint64_t g2 = e ? f2_pack(v.z, v.w) : f2_pack(v.x, v.y);
+        const uint64_t y2 = e ? f2_pack(h3.z, h3.w) : f2_pack(h3.x, h3.y);
+        float ta, tb;
+        f2_unpack(f2_mul(x2, nl2), ta, tb);
+        f2_unpack(f2_add(f2_pack(ex2_approx(ta), ex2_approx(tb)), one2), ta, tb);
+        const uint64_t sig = f2_pack(rcp_approx(ta), rcp_approx(tb));
+        const uint64_t d3 = f2_mul(g2, f2_mul(x2, sig));                  // dg * silu(h1)
+        const uint64_t q = f2_fma(x2, f2_sub(one2, sig), one2);            // 1 + h1 (1 - sig)
+        const uint64_t d1 = f2_mul(f2_mul(g2, y2), f2_mul(sig, q));        // dg h3 sig (1 + h1 (1 - sig))
+        f2_unpack(d1, ta, tb);
+        o1[e] = pack_bf16x2(ta, tb);
+        f2_unpack(d3, ta, tb);
+        o3[e] = pack_bf16x2(ta, tb);
       }
       __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + mr * p.ldo;
-      *reinterpret_cast<uint2*>(o + col) = pack_bf16x4(make_float4(d1[0], d1[1], d1[2], d1[3]));
-      *reinterpret_cast<uint2*>(o + p.n_half + col) = pack_bf16x4(make_float4(d3[0], d3[1], d3[2], d3[3]));
+      *reinterpret_cast<uint2*>(o + col) = make_uint2(o1[0], o1[1]);
+      *reinterpret_cast<uint2*>(o + p.n_half + col) = make_uint2(o3[0], o3[1]);
     }
   }
 }
